@@ -1,0 +1,82 @@
+"""Generate the golden vectors by running the REFERENCE optimizer on the CPU.
+
+Run once, in a container where the reference checkout exists:
+
+    python tests/golden/make_golden.py [--ref /root/reference] [case ...]
+
+For every case of cases.py it builds the seeded synthetic params, runs the
+reference's own ``SMO8bit`` / ``SMO`` (smo/optimizers/spatial_8bit.py,
+smo/optimizers/spatial.py) for the case's steps with the seeded synthetic
+grads, and writes ``<case>.npz`` next to this script: the final optimizer
+state arrays, the state metadata, and the final params (a strided sample for
+the large single-weight case).  The tests compare the CPU oracle and the CUDA
+library against these files; nothing at test time imports the reference.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("cases", nargs="*")
+    args = ap.parse_args()
+
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, args.ref)
+    import torch
+    from smo.optimizers.spatial import SMO
+    from smo.optimizers.spatial_8bit import SMO8bit
+
+    sys.path.insert(0, HERE)
+    import cases as C
+
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    names = args.cases or list(C.CASES)
+    for name in names:
+        case = C.CASES[name]
+        params = [torch.nn.Parameter(torch.from_numpy(a.copy())) for a in C.case_params(case)]
+        groups = C.case_groups(case, params)
+        cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
+        opt = cls(groups, **case["kwargs"])
+        for step in range(1, case["steps"] + 1):
+            for p, g in zip(params, C.case_grads(case, step)):
+                p.grad = torch.from_numpy(g.copy())
+            opt.step()
+        out = {}
+        meta = {"case": name, "torch": torch.__version__, "tensors": []}
+        stride = case.get("sample_stride")
+        for i, p in enumerate(params):
+            arr = p.detach().numpy().reshape(-1)
+            if stride:
+                out[f"{i}.param_sample"] = arr[C.sample_indices(arr.size, stride)].copy()
+            else:
+                out[f"{i}.param"] = arr.copy()
+            st = opt.state[p]
+            tmeta = {}
+            for k in C.STATE_META_KEYS:
+                if k in st:
+                    v = st[k]
+                    tmeta[k] = list(v) if isinstance(v, tuple) else v
+            meta["tensors"].append(tmeta)
+            for k in C.STATE_ARRAY_KEYS:
+                if k in st:
+                    out[f"{i}.{k}"] = st[k].detach().numpy().copy()
+        out["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+        path = os.path.join(HERE, f"{name}.npz")
+        np.savez_compressed(path, **out)
+        print(f"{name}: {os.path.getsize(path) / 1024:.1f} KiB")
+
+
+if __name__ == "__main__":
+    main()
