@@ -1,0 +1,410 @@
+#!/usr/bin/env python
+"""Throughput of the SMO8bit optimizer step on B200 (params stepped/s, HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+One "step" is one optimizer step over the whole parameter set of the workload
+(default: the ~700M-parameter decoder, SMO8bit k=0.25 low_peak, fp32 params,
+synthetic grads ~N(0, 1e-3)).  With N > 1 (launched by torch.distributed.run)
+the tensors are sharded ZeRO-1 style: each rank steps the tensors it owns, and
+``value`` is all ranks' params / the slowest rank's device time.  The NCCL
+broadcast of updated params that completes a ZeRO-1 step is timed separately
+(``zero1``).  Rank 0 prints one JSON line.
+
+``--impl reference`` times the CPU restatement of the reference step (the
+oracle, all host threads) on the same workload, one tensor per step in
+round-robin order, and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "params stepped/sec per SMO-8bit step"
+UNIT = "params/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="decoder700m")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic(workload, kernel):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            data = json.load(f)
+        return data[workload][kernel]
+    except Exception:
+        return None
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def build_workload(wl, seed, device, owned):
+    """Params (all tensors) and grads (owned tensors) filled on the device by the synthetic generator."""
+    import torch
+    from smo_optimizer_b200 import ops, synthetic
+
+    params, grads = [], []
+    for i, (name, shape) in enumerate(wl.tensors):
+        p = torch.empty(shape, dtype=torch.float32, device=device)
+        ops.synth_normal_(p, seed, synthetic.stream_id(synthetic.STREAM_PARAM, 0, i), 0.02)
+        params.append(torch.nn.Parameter(p))
+        if owned[i]:
+            g = torch.empty(shape, dtype=torch.float32, device=device)
+            ops.synth_normal_(g, seed, synthetic.stream_id(synthetic.STREAM_GRAD, 1, i), 1e-3)
+            if wl.bf16_grads:
+                g = g.to(torch.bfloat16).to(torch.float32)
+            params[-1].grad = g
+        grads.append(params[-1].grad)
+    return params, grads
+
+
+def cpu_baseline(wl, seed, seconds):
+    """The oracle (CPU restatement of the reference step) on a sample of the workload."""
+    import numpy as np
+
+    from oracle import oracle
+    from smo_optimizer_b200 import synthetic, zero
+
+    oracle.build()
+    # one decoder layer's tensors (or the first few of another workload)
+    take = []
+    total = 0
+    for i, (name, shape) in enumerate(wl.tensors):
+        take.append((i, shape))
+        total += int(np.prod(shape))
+        if total >= 25_000_000:
+            break
+    params = [synthetic.synth_param(seed, i, s) for i, s in take]
+    grads = [synthetic.synth_grad(seed, 1, i, s, bf16=wl.bf16_grads) for i, s in take]
+    opt = oracle.OracleOptimizer(wl.optimizer, [{"params": params}], **wl.kwargs)
+    opt.step(grads)  # warm-up (init + first step)
+    steps, t0 = 0, time.perf_counter()
+    while True:
+        opt.step(grads)
+        steps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or steps >= 1000:
+            break
+    return {"value": total * steps / el, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{len(take)} tensors ({total / 1e6:.1f}M params) of {wl.name}, {steps} steps, "
+                      f"{el:.1f} s, OpenMP C oracle"}
+
+
+def run_reference(args, rank, world):
+    """CPU restatement of the reference step (the oracle) on the host cores."""
+    if rank != 0:
+        return 0
+    import numpy as np
+
+    from oracle import oracle
+    from smo_optimizer_b200 import synthetic, workloads
+
+    oracle.build()
+    wl = workloads.WORKLOADS[args.workload]
+    n = len(wl.tensors)
+    # every tensor gets its own oracle optimizer so one step can touch one tensor
+    cache = {}
+
+    def tensor_opt(i):
+        if i not in cache:
+            shape = wl.tensors[i][1]
+            p = synthetic.synth_param(args.seed, i, shape)
+            g = synthetic.synth_grad(args.seed, 1, i, shape, bf16=wl.bf16_grads)
+            o = oracle.OracleOptimizer(wl.optimizer, [{"params": [p]}], **wl.kwargs)
+            o.step([g])  # lazy state init outside the timed region
+            cache.clear()
+            cache[i] = (o, g, int(np.prod(shape)))
+        return cache[i]
+
+    for w in range(args.warmup):
+        o, g, _ = tensor_opt(w % n)
+        o.step([g])
+    stepped, el = 0, 0.0
+    for k in range(args.steps):
+        o, g, numel = tensor_opt((args.warmup + k) % n)
+        t0 = time.perf_counter()
+        o.step([g])
+        el += time.perf_counter() - t0
+        stepped += numel
+    value = stepped / el
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32+int8",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "params": wl.numel, "tensors": n, **_cfg(wl)},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+                         "sample": f"one tensor of {wl.name} per step, round robin ({stepped / 1e6:.0f}M params)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _cfg(wl):
+    kw = wl.kwargs
+    cfg = {"optimizer": wl.optimizer, "k_ratio": kw.get("k_ratio"), "block_size": kw.get("block_size"),
+           "low_peak": kw.get("low_peak", False), "weight_decay": kw.get("weight_decay"),
+           "protect_output": wl.protect_output, "bf16_grads": wl.bf16_grads}
+    return cfg
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from smo_optimizer_b200 import SMO, SMO8bit, _lib, workloads, zero
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
+    wl = workloads.WORKLOADS[args.workload]
+    cls = SMO8bit if wl.optimizer == "SMO8bit" else SMO
+    kw = dict(wl.kwargs)
+
+    shapes = [s for _, s in wl.tensors]
+    costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64)) for s in shapes]
+    owner = zero.lpt_partition(costs, world)
+    owned = [o == rank for o in owner]
+    params, grads = build_workload(wl, args.seed, device, owned)
+    mine = [p for p, o in zip(params, owned) if o]
+    if wl.protect_output:
+        named = [(n, p) for (n, _), p, o in zip(wl.tensors, params, owned) if o]
+        opt = cls(named, protect_output=wl.protect_output, **kw)
+    else:
+        opt = cls(mine, **kw)
+    my_params = sum(p.numel() for p in mine)
+    my_bytes = sum(c for c, o in zip(costs, owned) if o)
+    total_params = wl.numel
+    lib = _lib.load()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    # ---- warm-up
+    for _ in range(max(3, args.warmup)):
+        opt.step()
+    torch.cuda.synchronize()
+    status = opt.workspace_status()
+    if status:
+        raise RuntimeError(f"device status {status} after warm-up")
+
+    # ---- timed region: device events, per-step events bracket the launch(es)
+    K = args.steps
+    stream = torch.cuda.current_stream()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local_rank)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    launches0 = lib.smo_launch_count()
+    t_start.record(stream)
+    for k in range(K):
+        ev[k][0].record(stream)
+        opt.step()
+        ev[k][1].record(stream)
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.smo_launch_count() - launches0
+    barrier()
+    clk = clocks.stop()
+    elapsed_ms = t_start.elapsed_time(t_end)
+    kern_ms = [a.elapsed_time(b) for a, b in ev]
+    step_ms_local = sum(kern_ms) / K
+    if world > 1:
+        t = torch.tensor([elapsed_ms, step_ms_local], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms, step_ms = float(t[0]), float(t[1])
+    else:
+        step_ms = step_ms_local
+    status = opt.workspace_status()
+    if status:
+        raise RuntimeError(f"device status {status} after the timed region")
+
+    ms_per_step = elapsed_ms / K
+    value = total_params / (ms_per_step * 1e-3)
+    peak, peak_src = load_peaks()
+    achieved = my_bytes / (step_ms_local * 1e-3) / 1e9
+    roof = {"bound": "hbm", "kernel": "smo step (all launches of one step)", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
+            "algorithmic_bytes_per_launch": my_bytes, "traffic": load_traffic(wl.name, "step")}
+
+    # ---- ZeRO-1 completion: broadcast of updated params from their owners
+    zero1 = None
+    if world > 1:
+        z = zero.Zero1.__new__(zero.Zero1)
+        z.group, z.world, z.rank, z.params, z.owner = None, world, rank, params, owner
+        for _ in range(3):
+            z.broadcast_params()
+        torch.cuda.synchronize()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nb = 10
+        a.record(stream)
+        for _ in range(nb):
+            opt.step()
+            z.broadcast_params()
+        b.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / nb], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        zms = float(t[0])
+        zero1 = {"step_plus_broadcast_ms": zms, "params_per_s": total_params / (zms * 1e-3),
+                 "broadcast_bytes_per_rank": 4 * (total_params - my_params)}
+
+    # ---- e2e through the public API with host buffers (pinned): H2D grads, step, D2H params
+    e2e = None
+    if not args.no_e2e:
+        host_g = [g.detach().cpu().pin_memory() for g, o in zip(grads, owned) if o]
+        dev_g = [g for g, o in zip(grads, owned) if o]
+        host_p = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in mine]
+        h2d = sum(g.numel() * 4 for g in host_g)
+        d2h = sum(p.numel() * 4 for p in mine)
+        KE = args.e2e_steps
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(KE):
+            for dg, hg in zip(dev_g, host_g):
+                dg.copy_(hg, non_blocking=True)
+            opt.step()
+            for hp_, p in zip(host_p, mine):
+                hp_.copy_(p.detach(), non_blocking=True)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ems = a.elapsed_time(b) / KE
+        if world > 1:
+            t = torch.tensor([ems], device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ems = float(t[0])
+        e2e = {"value": total_params / (ems * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": ems, "steps": KE,
+               "path": "SMO8bit.step() via the C ABI; pinned host grads H2D and params D2H each step"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(wl, args.seed, args.cpu_sample_seconds)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32+int8", "data": "synthetic (seeded counter-hash N(0,0.02) params, N(0,1e-3) grads)",
+            "config": {"workload": wl.name, "params": total_params, "tensors": len(wl.tensors),
+                       "parallelism": f"zero1-dp{world}" if world > 1 else "single", **_cfg(wl),
+                       "l2": "inputs (>= 6 GB) larger than L2; no flush"},
+            "hbm_gbs": sum(costs) / (ms_per_step * 1e-3) / 1e9,
+            "kernel_ms_per_step": step_ms,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "impl": "ours",
+        }
+        if zero1:
+            line["zero1"] = zero1
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

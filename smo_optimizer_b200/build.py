@@ -1,0 +1,85 @@
+"""Build recipe of the CUDA library (``libsmo_b200.so``, in-tree).
+
+    python -m smo_optimizer_b200.build [--verbose]
+
+Compiles every ``csrc/*.cu`` for sm_100a with nvcc into one shared library
+with the C ABI of include/smo_b200.h.  Needs nvcc only (no GPU): it
+cross-compiles.  ``-fmad=false`` keeps every multiply and add separately
+rounded unless the source asks for a fused multiply-add explicitly; the fp32
+op order must match the reference bit for bit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import glob
+import os
+import shutil
+import subprocess
+import sys
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(PKG)
+CSRC = os.path.join(PKG, "csrc")
+INCLUDE = os.path.join(ROOT, "include")
+LIB_PATH = os.path.join(PKG, "libsmo_b200.so")
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC,-O2",
+              "-Xcompiler", "-fvisibility=hidden"]
+
+
+def nvcc_path() -> str:
+    cand = os.environ.get("CUDA_HOME") or "/usr/local/cuda"
+    p = os.path.join(cand, "bin", "nvcc")
+    if os.path.exists(p):
+        return p
+    found = shutil.which("nvcc")
+    if not found:
+        raise RuntimeError("nvcc not found: the CUDA library cannot be built")
+    return found
+
+
+def sources():
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+
+
+def deps():
+    return sources() + sorted(glob.glob(os.path.join(CSRC, "*.cuh"))) + [os.path.join(INCLUDE, "smo_b200.h")]
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(LIB_PATH):
+        return False
+    t = os.path.getmtime(LIB_PATH)
+    return all(os.path.getmtime(d) <= t for d in deps())
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and up_to_date():
+        return LIB_PATH
+    tmp = LIB_PATH + ".tmp"
+    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-shared", "-o", tmp, *sources()]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd))
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("nvcc failed to build libsmo_b200.so")
+    if verbose:
+        sys.stderr.write(res.stderr)
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--force", action="store_true")
+    args = ap.parse_args()
+    print(build(force=args.force or args.verbose, verbose=args.verbose))
+
+
+if __name__ == "__main__":
+    main()

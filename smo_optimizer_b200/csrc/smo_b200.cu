@@ -1,0 +1,596 @@
+// smo_b200.cu -- C ABI, launchers and the general (any-shape) step kernels.
+//
+// The step over a batch of tensors runs as two launches:
+//   step_a_kernel  one warp per work item:
+//                    pooled kinds: one int8 block (or 64 cells) of the compact
+//                      grid: window sums of x = g + wd*p and x*x, dequant, EMA,
+//                      block absmax, requant; post-EMA fp32 moments go to the
+//                      compact buffers that step_b reads;
+//                    QUANT_ONLY: one int8 block of elements, EMA, requant, write;
+//                    DENSE: 1024 elements, EMA, write.
+//   step_b_kernel  one warp per full-resolution row of a pooled tensor:
+//                    bilinear reconstruction of m, v, clamp, Adam write.
+// The fused single-pass kernel for exact-window pooled tensors lives in
+// smo_fused.cu and is chosen by the launcher when a tensor qualifies.
+#include <atomic>
+#include <cstdio>
+#include <cstring>
+#include <cuda_runtime.h>
+
+#include "smo_common.cuh"
+#include "smo_internal.cuh"
+
+using namespace smo;
+
+namespace smo {
+
+thread_local int g_last_cuda_error = 0;
+std::atomic<uint64_t> g_launches{0};
+
+static int cuda_fail(cudaError_t e) {
+    g_last_cuda_error = (int)e;
+    return SMO_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------- kernels
+
+__device__ __forceinline__ int find_tensor(const int64_t *start, int n, int64_t item) {
+    int lo = 0, hi = n - 1;
+    while (lo < hi) {
+        int mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
+    const int64_t C = d.h * d.w;
+    const bool q8 = (d.kind == SMO_KIND_POOLED8);
+    const int64_t BI = q8 ? d.B : kPooled32Chunk;
+    const int64_t base = item * BI;
+    const smo_hyper &hp = d.hp;
+    float tm = 0.0f, tv = 0.0f;
+    if (q8) {
+        tm = dequant_step(d.ms_in[item]);
+        tv = dequant_step(d.vs_in[item]);
+    }
+    float am = 0.0f, av = 0.0f;
+    for (int64_t k = lane; k < BI; k += 32) {
+        int64_t c = base + k;
+        if (c >= C) break;
+        int64_t i = c / d.w, j = c - i * d.w;
+        float gm, g2;
+        pool_cell(d.g, d.p, d.H, d.W, d.h, d.w, d.exact, i, j, hp, gm, g2);
+        float m, v;
+        if (q8) {
+            m = dequant1(d.mq_in[c], tm);
+            v = dequant1(d.vq_in[c], tv);
+        } else {
+            m = d.m_in[c];
+            v = d.v_in[c];
+        }
+        m = ema(m, gm, hp.beta1, hp.omb1);
+        v = ema(v, g2, hp.beta2, hp.omb2);
+        d.m_out[c] = m;
+        d.v_out[c] = v;
+        am = absmax_acc(am, m);
+        av = absmax_acc(av, v);
+    }
+    if (!q8) return;
+    const float sm = block_scale(warp_absmax(am));
+    const float sv = block_scale(warp_absmax(av));
+    for (int64_t k = lane; k < BI; k += 32) {
+        int64_t c = base + k;
+        float m = 0.0f, v = 0.0f;
+        if (c < C) {
+            m = d.m_out[c];
+            v = d.v_out[c];
+        }
+        d.mq_out[c] = quantize1(m, sm);
+        d.vq_out[c] = quantize1(v, sv);
+    }
+    if (lane == 0) {
+        d.ms_out[item] = sm;
+        d.vs_out[item] = sv;
+    }
+}
+
+__device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
+    const int64_t N = d.H;
+    const int64_t B = d.B;
+    const int64_t base = item * B;
+    const smo_hyper &hp = d.hp;
+    const float tm = dequant_step(d.ms_in[item]);
+    const float tv = dequant_step(d.vs_in[item]);
+    float am = 0.0f, av = 0.0f;
+    for (int64_t k = lane; k < B; k += 32) {
+        int64_t i = base + k;
+        if (i >= N) break;
+        float x = decayed(d.g[i], d.p[i], hp);
+        float m = ema(dequant1(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
+        float v = ema_sq(dequant1(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
+        am = absmax_acc(am, m);
+        av = absmax_acc(av, v);
+    }
+    const float sm = block_scale(warp_absmax(am));
+    const float sv = block_scale(warp_absmax(av));
+    for (int64_t k = lane; k < B; k += 32) {
+        int64_t i = base + k;
+        if (i < N) {
+            float p = d.p[i];
+            float x = decayed(d.g[i], p, hp);
+            float m = ema(dequant1(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
+            float v = ema_sq(dequant1(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
+            d.mq_out[i] = quantize1(m, sm);
+            d.vq_out[i] = quantize1(v, sv);
+            d.p[i] = adam_write(p, m, v, hp);
+        } else {
+            d.mq_out[i] = 0;
+            d.vq_out[i] = 0;
+        }
+    }
+    if (lane == 0) {
+        d.ms_out[item] = sm;
+        d.vs_out[item] = sv;
+    }
+}
+
+__device__ void dense_item(const DevDesc &d, int64_t item, int lane) {
+    const int64_t N = d.H;
+    const int64_t base = item * kDenseChunk;
+    const int64_t end = base + kDenseChunk < N ? base + kDenseChunk : N;
+    const smo_hyper &hp = d.hp;
+    for (int64_t i = base + lane; i < end; i += 32) {
+        float p = d.p[i];
+        float x = decayed(d.g[i], p, hp);
+        float m = ema(d.m_in[i], x, hp.beta1, hp.omb1);
+        float v = ema_sq(d.v_in[i], x, hp.beta2, hp.omb2);
+        d.m_out[i] = m;
+        d.v_out[i] = v;
+        d.p[i] = adam_write(p, m, v, hp);
+    }
+}
+
+__global__ void __launch_bounds__(256) step_a_kernel(const __grid_constant__ Batch b) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t total = b.start_a[b.n];
+    for (int64_t it = warp; it < total; it += nwarps) {
+        const int t = find_tensor(b.start_a, b.n, it);
+        const DevDesc &d = b.d[t];
+        const int64_t item = it - b.start_a[t];
+        switch (d.kind) {
+            case SMO_KIND_POOLED8:
+            case SMO_KIND_POOLED32: pooled_block_item(d, item, lane); break;
+            case SMO_KIND_QUANT_ONLY: quant_only_item(d, item, lane); break;
+            case SMO_KIND_DENSE: dense_item(d, item, lane); break;
+            default: break;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) step_b_kernel(const __grid_constant__ Batch b) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    const int64_t total = b.start_b[b.n];
+    for (int64_t it = warp; it < total; it += nwarps) {
+        const int t = find_tensor(b.start_b, b.n, it);
+        const DevDesc &d = b.d[t];
+        const int64_t r = it - b.start_b[t];
+        int small;
+        const Coef rc = row_coef(r, d.H, d.h, d.W, d.band, small);
+        float *prow = d.p + r * d.W;
+        for (int64_t q = lane; q < d.W; q += 32) {
+            float mh, vh;
+            if (d.same) {
+                mh = d.m_out[r * d.w + q];
+                vh = d.v_out[r * d.w + q];
+            } else {
+                const Coef cc = coef_for(q, d.w, d.W);
+                if (small) {
+                    mh = interp_small(d.m_out, d.w, rc, cc);
+                    vh = interp_small(d.v_out, d.w, rc, cc);
+                } else {
+                    mh = interp_generic(d.m_out, d.w, rc, cc, r, q);
+                    vh = interp_generic(d.v_out, d.w, rc, cc, r, q);
+                }
+            }
+            prow[q] = adam_write(prow[q], mh, clamp_min0(vh), d.hp);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- stage kernels
+
+__global__ void quantize_kernel(const float *__restrict__ x, int64_t n, int64_t B, int8_t *codes, float *scales,
+                                int64_t nb) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t b = warp; b < nb; b += nwarps) {
+        float am = 0.0f;
+        for (int64_t k = lane; k < B; k += 32) {
+            int64_t i = b * B + k;
+            if (i >= n) break;
+            am = absmax_acc(am, x[i]);
+        }
+        const float s = block_scale(warp_absmax(am));
+        for (int64_t k = lane; k < B; k += 32) {
+            int64_t i = b * B + k;
+            codes[i] = quantize1(i < n ? x[i] : 0.0f, s);
+        }
+        if (lane == 0) scales[b] = s;
+    }
+}
+
+__global__ void dequantize_kernel(const int8_t *__restrict__ codes, const float *__restrict__ scales, int64_t n,
+                                  int64_t B, float *out) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        out[i] = dequant1(codes[i], dequant_step(scales[i / B]));
+}
+
+__global__ void pool_kernel(const float *__restrict__ g, const float *__restrict__ p, int64_t H, int64_t W,
+                            int64_t h, int64_t w, int exact, smo_hyper hp, float *om, float *o2) {
+    const int64_t C = h * w;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < C; c += (int64_t)gridDim.x * blockDim.x) {
+        int64_t i = c / w, j = c - i * w;
+        pool_cell(g, p, H, W, h, w, exact, i, j, hp, om[c], o2[c]);
+    }
+}
+
+__global__ void upsample_kernel(const float *__restrict__ src, int64_t h, int64_t w, int64_t H, int64_t W,
+                                int64_t band, float *out) {
+    const int64_t N = H * W;
+    const int same = (h == H && w == W && band <= 0);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < N; e += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = e / W, q = e - r * W;
+        if (same) { out[e] = src[r * w + q]; continue; }
+        int small;
+        const Coef rc = row_coef(r, H, h, W, band, small);
+        const Coef cc = coef_for(q, w, W);
+        out[e] = small ? interp_small(src, w, rc, cc) : interp_generic(src, w, rc, cc, r, q);
+    }
+}
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void synth_normal_kernel(float *out, int64_t n, uint64_t base, float scale, int64_t offset) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        uint64_t idx = (uint64_t)(offset + i);
+        uint64_t ha = splitmix64(base + 2ull * idx);
+        uint64_t hb = splitmix64(base + 2ull * idx + 1ull);
+        int64_t s = 0;
+#pragma unroll
+        for (int k = 0; k < 4; k++) s += (int64_t)((ha >> (16 * k)) & 0xFFFFull) + (int64_t)((hb >> (16 * k)) & 0xFFFFull);
+        out[i] = __fmul_rn((float)(2 * s - 8 * 65535), scale);
+    }
+}
+
+__global__ void selftest_wait_kernel(const unsigned int *flag, int64_t max_iters, int32_t *status) {
+    // Nothing sets *flag: the bounded wait must give up and report a timeout.
+    int st = bounded_wait_geq(flag, 1u, max_iters) ? SMO_OK : SMO_ERR_TIMEOUT;
+    if (threadIdx.x == 0 && blockIdx.x == 0) *status = st;
+}
+
+// ---------------------------------------------------------------- host side
+
+static int device_sms() {
+    static thread_local int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) sms = 148;
+    }
+    return sms;
+}
+
+static inline bool aligned(const void *ptr, size_t a) { return ((uintptr_t)ptr % a) == 0; }
+
+// Validates one ABI descriptor and fills the device descriptor; scratch
+// offsets for POOLED8 post-EMA moments are assigned by the caller.
+static int make_desc(const smo_tensor &t, DevDesc &d) {
+    memset(&d, 0, sizeof(d));
+    if (!t.param || !t.grad) return SMO_ERR_INVALID;
+    if (!aligned(t.param, 4) || !aligned(t.grad, 4)) return SMO_ERR_ALIGNMENT;
+    d.p = t.param;
+    d.g = t.grad;
+    d.kind = t.kind;
+    d.hp = t.hp;
+    d.H = t.rows;
+    d.W = t.cols;
+    switch (t.kind) {
+        case SMO_KIND_POOLED8:
+        case SMO_KIND_POOLED32: {
+            if (t.rows <= 0 || t.cols <= 0 || t.comp_rows <= 0 || t.comp_cols <= 0) return SMO_ERR_INVALID;
+            if (t.comp_rows > t.rows || t.comp_cols > t.cols) return SMO_ERR_INVALID;
+            d.h = t.comp_rows;
+            d.w = t.comp_cols;
+            d.exact = (t.rows % t.comp_rows == 0 && t.cols % t.comp_cols == 0);
+            d.band = t.interp_band;
+            if (d.band < 0 || (d.band > 0 && !d.exact)) return SMO_ERR_INVALID;
+            d.same = (d.h == d.H && d.w == d.W && d.band == 0);
+            if (t.kind == SMO_KIND_POOLED8) {
+                if (t.q_block <= 0) return SMO_ERR_INVALID;
+                if (!t.m_q_in || !t.m_s_in || !t.v_q_in || !t.v_s_in || !t.m_q_out || !t.m_s_out || !t.v_q_out ||
+                    !t.v_s_out)
+                    return SMO_ERR_INVALID;
+                if (!aligned(t.m_s_in, 4) || !aligned(t.v_s_in, 4) || !aligned(t.m_s_out, 4) ||
+                    !aligned(t.v_s_out, 4))
+                    return SMO_ERR_ALIGNMENT;
+                d.B = t.q_block;
+                d.mq_in = t.m_q_in; d.ms_in = t.m_s_in; d.vq_in = t.v_q_in; d.vs_in = t.v_s_in;
+                d.mq_out = t.m_q_out; d.ms_out = t.m_s_out; d.vq_out = t.v_q_out; d.vs_out = t.v_s_out;
+            } else {
+                if (!t.m_in || !t.v_in || !t.m_out || !t.v_out) return SMO_ERR_INVALID;
+                if (!aligned(t.m_in, 4) || !aligned(t.v_in, 4) || !aligned(t.m_out, 4) || !aligned(t.v_out, 4))
+                    return SMO_ERR_ALIGNMENT;
+                d.m_in = t.m_in; d.v_in = t.v_in; d.m_out = t.m_out; d.v_out = t.v_out;
+            }
+            return SMO_OK;
+        }
+        case SMO_KIND_DENSE:
+            if (t.rows < 0 || t.cols != 1) return SMO_ERR_INVALID;
+            if (!t.m_in || !t.v_in || !t.m_out || !t.v_out) return SMO_ERR_INVALID;
+            if (!aligned(t.m_in, 4) || !aligned(t.v_in, 4) || !aligned(t.m_out, 4) || !aligned(t.v_out, 4))
+                return SMO_ERR_ALIGNMENT;
+            d.m_in = t.m_in; d.v_in = t.v_in; d.m_out = t.m_out; d.v_out = t.v_out;
+            return SMO_OK;
+        case SMO_KIND_QUANT_ONLY:
+            if (t.rows < 0 || t.cols != 1 || t.q_block <= 0) return SMO_ERR_INVALID;
+            if (!t.m_q_in || !t.m_s_in || !t.v_q_in || !t.v_s_in || !t.m_q_out || !t.m_s_out || !t.v_q_out ||
+                !t.v_s_out)
+                return SMO_ERR_INVALID;
+            if (!aligned(t.m_s_in, 4) || !aligned(t.v_s_in, 4) || !aligned(t.m_s_out, 4) || !aligned(t.v_s_out, 4))
+                return SMO_ERR_ALIGNMENT;
+            d.B = t.q_block;
+            d.mq_in = t.m_q_in; d.ms_in = t.m_s_in; d.vq_in = t.v_q_in; d.vs_in = t.v_s_in;
+            d.mq_out = t.m_q_out; d.ms_out = t.m_s_out; d.vq_out = t.v_q_out; d.vs_out = t.v_s_out;
+            return SMO_OK;
+        default:
+            return SMO_ERR_INVALID;
+    }
+}
+
+static inline int64_t items_a(const DevDesc &d) {
+    switch (d.kind) {
+        case SMO_KIND_POOLED8: return (d.h * d.w + d.B - 1) / d.B;
+        case SMO_KIND_POOLED32: return (d.h * d.w + kPooled32Chunk - 1) / kPooled32Chunk;
+        case SMO_KIND_QUANT_ONLY: return (d.H + d.B - 1) / d.B;
+        case SMO_KIND_DENSE: return (d.H + kDenseChunk - 1) / kDenseChunk;
+        default: return 0;
+    }
+}
+
+static inline int64_t items_b(const DevDesc &d) {
+    return (d.kind == SMO_KIND_POOLED8 || d.kind == SMO_KIND_POOLED32) ? d.H : 0;
+}
+
+static inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// scratch bytes of the general path for one tensor (POOLED8 post-EMA moments)
+static inline size_t general_scratch(const smo_tensor &t) {
+    if (t.kind != SMO_KIND_POOLED8) return 0;
+    return 2 * round_up((size_t)t.comp_rows * (size_t)t.comp_cols * sizeof(float), kScratchAlign);
+}
+
+static int launch_general(Batch &b, cudaStream_t stream) {
+    b.start_a[0] = 0;
+    b.start_b[0] = 0;
+    for (int i = 0; i < b.n; i++) {
+        b.start_a[i + 1] = b.start_a[i] + items_a(b.d[i]);
+        b.start_b[i + 1] = b.start_b[i] + items_b(b.d[i]);
+    }
+    const int threads = 256, warps = threads / 32;
+    const int64_t cap = (int64_t)device_sms() * 16;
+    if (b.start_a[b.n] > 0) {
+        int64_t blocks = (b.start_a[b.n] + warps - 1) / warps;
+        blocks = blocks < cap ? blocks : cap;
+        step_a_kernel<<<(unsigned)blocks, threads, 0, stream>>>(b);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e);
+        g_launches++;
+    }
+    if (b.start_b[b.n] > 0) {
+        int64_t blocks = (b.start_b[b.n] + warps - 1) / warps;
+        blocks = blocks < cap ? blocks : cap;
+        step_b_kernel<<<(unsigned)blocks, threads, 0, stream>>>(b);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e);
+        g_launches++;
+    }
+    return SMO_OK;
+}
+
+}  // namespace smo
+
+// ===================================================================== C ABI
+
+extern "C" {
+
+size_t smo_workspace_size(const smo_tensor *tensors, int32_t n) {
+    if (!tensors || n <= 0) return 0;
+    size_t general = 0;
+    for (int32_t i = 0; i < n; i++) general += general_scratch(tensors[i]);
+    size_t fused = fused_workspace_size(tensors, n);
+    size_t body = general > fused ? general : fused;
+    return body ? kWsHeader + body : kWsHeader;
+}
+
+int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t workspace_bytes, void *stream_ptr) {
+    if (n < 0 || (n > 0 && !tensors)) return SMO_ERR_INVALID;
+    if (n == 0) return SMO_OK;
+    cudaStream_t stream = (cudaStream_t)stream_ptr;
+
+    // Validate everything before any launch: a bad descriptor launches nothing.
+    static thread_local Batch batch;
+    for (int32_t i = 0; i < n; i++) {
+        DevDesc d;
+        int st = make_desc(tensors[i], d);
+        if (st != SMO_OK) return st;
+    }
+    const size_t need = smo_workspace_size(tensors, n);
+    if (!workspace || workspace_bytes < need || !aligned(workspace, kScratchAlign)) return SMO_ERR_WORKSPACE;
+    char *ws = (char *)workspace;
+
+    // Tensors the fused single-pass kernel takes (exact-window pooled shapes).
+    int st = fused_step(tensors, n, ws, workspace_bytes, stream);
+    if (st != SMO_OK) return st;
+
+    // Everything else goes through the general two-launch path, batched.
+    size_t off = kWsHeader;
+    batch.n = 0;
+    for (int32_t i = 0; i < n; i++) {
+        if (fused_takes(tensors[i])) continue;
+        DevDesc &d = batch.d[batch.n];
+        make_desc(tensors[i], d);
+        if (d.kind == SMO_KIND_POOLED8) {
+            const size_t bytes = round_up((size_t)(d.h * d.w) * sizeof(float), kScratchAlign);
+            d.m_out = (float *)(ws + off);
+            d.v_out = (float *)(ws + off + bytes);
+            off += 2 * bytes;
+        }
+        batch.n++;
+        if (batch.n == kMaxBatch) {
+            st = launch_general(batch, stream);
+            if (st != SMO_OK) return st;
+            batch.n = 0;
+            off = kWsHeader;  // stream order: the next launch pair starts after this one ends
+        }
+    }
+    if (batch.n > 0) return launch_general(batch, stream);
+    return SMO_OK;
+}
+
+int smo_workspace_status(void *workspace, void *stream_ptr) {
+    if (!workspace) return SMO_ERR_WORKSPACE;
+    WsHeader h;
+    cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)stream_ptr);
+    if (e != cudaSuccess) return cuda_fail(e);
+    e = cudaStreamSynchronize((cudaStream_t)stream_ptr);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return h.error ? (int)h.error : SMO_OK;
+}
+
+int smo_quantize_blockwise(const float *x, int64_t n, int64_t block, int8_t *codes, float *scales, void *stream) {
+    if (n < 0 || block <= 0 || (n > 0 && (!x || !codes || !scales))) return SMO_ERR_INVALID;
+    if (n == 0) return SMO_OK;
+    const int64_t nb = (n + block - 1) / block;
+    int64_t blocks = (nb + 7) / 8;
+    const int64_t cap = (int64_t)device_sms() * 16;
+    blocks = blocks < cap ? blocks : cap;
+    quantize_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(x, n, block, codes, scales, nb);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_launches++;
+    return SMO_OK;
+}
+
+int smo_dequantize_blockwise(const int8_t *codes, const float *scales, int64_t n, int64_t block, float *out,
+                             void *stream) {
+    if (n < 0 || block <= 0 || (n > 0 && (!codes || !scales || !out))) return SMO_ERR_INVALID;
+    if (n == 0) return SMO_OK;
+    int64_t blocks = (n + 255) / 256;
+    const int64_t cap = (int64_t)device_sms() * 16;
+    blocks = blocks < cap ? blocks : cap;
+    dequantize_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(codes, scales, n, block, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_launches++;
+    return SMO_OK;
+}
+
+int smo_pool2d_pair(const float *grad, const float *param, int64_t H, int64_t W, int64_t h, int64_t w,
+                    float weight_decay, int32_t wd_on, float *out_mean, float *out_sq_mean, void *stream) {
+    if (H <= 0 || W <= 0 || h <= 0 || w <= 0 || h > H || w > W) return SMO_ERR_INVALID;
+    if (!grad || !out_mean || !out_sq_mean || (wd_on && !param)) return SMO_ERR_INVALID;
+    smo_hyper hp;
+    memset(&hp, 0, sizeof(hp));
+    hp.weight_decay = weight_decay;
+    hp.wd_on = wd_on ? 1 : 0;
+    const int exact = (H % h == 0 && W % w == 0);
+    int64_t blocks = (h * w + 255) / 256;
+    const int64_t cap = (int64_t)device_sms() * 16;
+    blocks = blocks < cap ? blocks : cap;
+    pool_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(grad, wd_on ? param : grad, H, W, h, w, exact,
+                                                                     hp, out_mean, out_sq_mean);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_launches++;
+    return SMO_OK;
+}
+
+int smo_upsample2d(const float *src, int64_t h, int64_t w, int64_t H, int64_t W, int64_t interp_band, float *out,
+                   void *stream) {
+    if (H <= 0 || W <= 0 || h <= 0 || w <= 0 || h > H || w > W || !src || !out) return SMO_ERR_INVALID;
+    if (interp_band < 0 || (interp_band > 0 && (H % h != 0))) return SMO_ERR_INVALID;
+    int64_t blocks = (H * W + 255) / 256;
+    const int64_t cap = (int64_t)device_sms() * 16;
+    blocks = blocks < cap ? blocks : cap;
+    upsample_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(src, h, w, H, W, interp_band, out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_launches++;
+    return SMO_OK;
+}
+
+int smo_synth_normal(float *out, int64_t n, uint64_t base, float scale, int64_t offset, void *stream) {
+    if (n < 0 || (n > 0 && !out)) return SMO_ERR_INVALID;
+    if (n == 0) return SMO_OK;
+    int64_t blocks = (n + 255) / 256;
+    const int64_t cap = (int64_t)device_sms() * 32;
+    blocks = blocks < cap ? blocks : cap;
+    synth_normal_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(out, n, base, scale, offset);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    g_launches++;
+    return SMO_OK;
+}
+
+int smo_selftest_wait_timeout(void *workspace, size_t workspace_bytes, int64_t max_iters, int32_t *status_out,
+                              void *stream_ptr) {
+    if (!status_out || max_iters < 0) return SMO_ERR_INVALID;
+    if (!workspace || workspace_bytes < kWsHeader || !aligned(workspace, kScratchAlign)) return SMO_ERR_WORKSPACE;
+    cudaStream_t stream = (cudaStream_t)stream_ptr;
+    // header words 32 (a flag nothing sets) and 33 (the status); the scheduler
+    // words of a later step are untouched
+    unsigned int *flag = (unsigned int *)workspace + 32;
+    cudaError_t e = cudaMemsetAsync(flag, 0, 2 * sizeof(unsigned int), stream);
+    if (e == cudaSuccess) {
+        selftest_wait_kernel<<<1, 32, 0, stream>>>(flag, max_iters, (int32_t *)(flag + 1));
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(status_out, flag + 1, sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? SMO_OK : cuda_fail(e);
+}
+
+const char *smo_status_string(int status) {
+    switch (status) {
+        case SMO_OK: return "ok";
+        case SMO_ERR_INVALID: return "invalid tensor descriptor";
+        case SMO_ERR_ALIGNMENT: return "misaligned pointer";
+        case SMO_ERR_WORKSPACE: return "workspace missing, misaligned or too small";
+        case SMO_ERR_CUDA: return "CUDA error";
+        case SMO_ERR_TIMEOUT: return "bounded device wait timed out";
+        case SMO_ERR_NONFINITE: return "non-finite value";
+        default: return "unknown status";
+    }
+}
+
+int smo_last_cuda_error(void) { return g_last_cuda_error; }
+
+uint64_t smo_launch_count(void) { return g_launches.load(); }
+
+int smo_abi_version(void) { return SMO_ABI_VERSION; }
+
+size_t smo_tensor_struct_size(void) { return sizeof(smo_tensor); }
+
+}  // extern "C"

@@ -1,0 +1,189 @@
+// smo_common.cuh -- shared device arithmetic of the SMO step.
+//
+// Every function here reproduces one fp32 operation sequence of the reference
+// step (as executed by torch's CPU kernels) with each rounding explicit:
+// __fmaf_rn where torch fuses a multiply-add, __fmul_rn / __fadd_rn /
+// __fdiv_rn / __fsqrt_rn where it rounds each operation.  The library is also
+// compiled with -fmad=false so that nothing else is contracted.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "smo_b200.h"
+
+namespace smo {
+
+// ---------------------------------------------------------------- scalars
+
+// x = g + wd * p  (grad.add(p, alpha=wd), spatial_8bit.py:217-218)
+__device__ __forceinline__ float decayed(float g, float p, const smo_hyper &hp) {
+    return hp.wd_on ? __fmaf_rn(hp.weight_decay, p, g) : g;
+}
+
+// m.mul_(b1).add_(u, alpha=1-b1)  (spatial_8bit.py:240-242)
+__device__ __forceinline__ float ema(float m, float u, float beta, float omb) {
+    return __fmaf_rn(omb, u, __fmul_rn(m, beta));
+}
+
+// v.mul_(b2).addcmul_(x, x, value=1-b2)  (spatial_8bit.py:281)
+__device__ __forceinline__ float ema_sq(float v, float x, float beta, float omb) {
+    return __fmaf_rn(__fmul_rn(omb, x), x, __fmul_rn(v, beta));
+}
+
+// denom = sqrt(v)/sqrt(bc2) + eps;  p.addcdiv_(m, denom, value=-step_size)
+// (spatial_8bit.py:293-297)
+__device__ __forceinline__ float adam_write(float p, float m, float v, const smo_hyper &hp) {
+    float d = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), hp.sqrt_bc2), hp.eps);
+    return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
+}
+
+// torch.clamp(v, min=0): NaN passes through (fmaxf would drop it)
+__device__ __forceinline__ float clamp_min0(float v) { return v < 0.0f ? 0.0f : v; }
+
+// NaN-propagating running max of |x| (torch's max reduction propagates NaN)
+__device__ __forceinline__ float absmax_acc(float acc, float x) {
+    float a = fabsf(x);
+    return (a > acc || a != a) ? a : acc;
+}
+
+__device__ __forceinline__ float warp_absmax(float acc) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float other = __shfl_xor_sync(0xffffffffu, acc, o);
+        acc = (other > acc || other != other) ? other : acc;
+    }
+    return acc;
+}
+
+// scales.clamp(min=1e-12) (spatial_8bit.py:96), NaN passes through
+__device__ __forceinline__ float block_scale(float absmax) { return absmax < 1e-12f ? 1e-12f : absmax; }
+
+// q = round(x / s * 127) half-to-even, dead-zone lift, clamp +-127
+// (spatial_8bit.py:97-106).  NaN is stored as 0.
+__device__ __forceinline__ int8_t quantize1(float x, float s) {
+    float r = rintf(__fmul_rn(__fdiv_rn(x, s), 127.0f));
+    if (r == 0.0f && x != 0.0f && x == x) r = x > 0.0f ? 1.0f : -1.0f;
+    r = r > 127.0f ? 127.0f : r;
+    r = r < -127.0f ? -127.0f : r;
+    return (r == r) ? (int8_t)(int)r : (int8_t)0;
+}
+
+// q * (s / 127)  (spatial_8bit.py:118)
+__device__ __forceinline__ float dequant_step(float s) { return __fdiv_rn(s, 127.0f); }
+__device__ __forceinline__ float dequant1(int8_t q, float t) { return __fmul_rn((float)q, t); }
+
+// ---------------------------------------------------------------- bilinear
+
+// torch's compute_source_index_and_lambda for align_corners=False
+struct Coef {
+    int64_t i0, i1;
+    float l0, l1;
+    int ident;  // equal extents: pass-through
+};
+
+__device__ __forceinline__ Coef coef_for(int64_t o, int64_t in, int64_t out) {
+    Coef c;
+    if (in == out) {
+        c.i0 = c.i1 = o;
+        c.l0 = 1.0f;
+        c.l1 = 0.0f;
+        c.ident = 1;
+        return c;
+    }
+    float scale = __fdiv_rn((float)in, (float)out);
+    float real = __fmaf_rn(scale, __fadd_rn((float)o, 0.5f), -0.5f);
+    real = real < 0.0f ? 0.0f : real;
+    int64_t i0 = (int64_t)floorf(real);
+    i0 = i0 > in - 1 ? in - 1 : i0;
+    float l1 = __fsub_rn(real, (float)i0);
+    l1 = l1 < 0.0f ? 0.0f : (l1 > 1.0f ? 1.0f : l1);
+    c.i0 = i0;
+    c.i1 = i0 + (i0 < in - 1 ? 1 : 0);
+    c.l1 = l1;
+    c.l0 = __fsub_rn(1.0f, l1);
+    c.ident = 0;
+    return c;
+}
+
+// Row coefficients; interp_band > 0 reproduces the low_peak bands of
+// spatial_8bit.py:359-370 (rows [a, b) interpolated onto (b-a)*kh rows).
+__device__ __forceinline__ Coef row_coef(int64_t r, int64_t H, int64_t h, int64_t W, int64_t band, int &small) {
+    if (band <= 0) {
+        small = (H + W <= 128);
+        return coef_for(r, h, H);
+    }
+    int64_t kh = H / h;
+    int64_t s0 = ((r / kh) / band) * band;
+    int64_t s1 = s0 + band < h ? s0 + band : h;
+    int64_t a = s0 > 0 ? s0 - 1 : 0;
+    int64_t b = s1 + 1 < h ? s1 + 1 : h;
+    int64_t n = b - a;
+    small = (n * kh + W <= 128);
+    Coef c = coef_for(r - a * kh, n, n * kh);
+    c.i0 += a;
+    c.i1 += a;
+    return c;
+}
+
+// torch's separable bilinear (output H+W > 128): width pass, then height pass
+__device__ __forceinline__ float interp_generic(const float *src, int64_t w, const Coef &rc, const Coef &cc,
+                                                int64_t r, int64_t q) {
+    if (rc.ident && cc.ident) return src[r * w + q];
+    if (rc.ident) {
+        const float *s = src + r * w;
+        return __fmaf_rn(s[cc.i0], cc.l0, __fmul_rn(s[cc.i1], cc.l1));
+    }
+    if (cc.ident) return __fmaf_rn(src[rc.i0 * w + q], rc.l0, __fmul_rn(src[rc.i1 * w + q], rc.l1));
+    const float *s0 = src + rc.i0 * w, *s1 = src + rc.i1 * w;
+    float t0 = __fmaf_rn(s0[cc.i0], cc.l0, __fmul_rn(s0[cc.i1], cc.l1));
+    float t1 = __fmaf_rn(s1[cc.i0], cc.l0, __fmul_rn(s1[cc.i1], cc.l1));
+    return __fmaf_rn(t0, rc.l0, __fmul_rn(t1, rc.l1));
+}
+
+// torch's channels-last bilinear kernel (used when output H+W <= 128)
+__device__ __forceinline__ float interp_small(const float *src, int64_t w, const Coef &rc, const Coef &cc) {
+    float w00 = __fmul_rn(rc.l0, cc.l0), w01 = __fmul_rn(rc.l0, cc.l1);
+    float w10 = __fmul_rn(rc.l1, cc.l0), w11 = __fmul_rn(rc.l1, cc.l1);
+    float a = src[rc.i0 * w + cc.i0], b = src[rc.i0 * w + cc.i1];
+    float c = src[rc.i1 * w + cc.i0], d = src[rc.i1 * w + cc.i1];
+    return __fmaf_rn(d, w11, __fmaf_rn(c, w10, __fmaf_rn(a, w00, __fmul_rn(b, w01))));
+}
+
+// ---------------------------------------------------------------- pooling
+
+// Window sums of x and x*x for compact cell (i, j): sequential row-major from
+// +0 (torch's cpu avg_pool2d / adaptive_avg_pool2d loops), then the divisions.
+__device__ __forceinline__ void pool_cell(const float *__restrict__ g, const float *__restrict__ p, int64_t H,
+                                          int64_t W, int64_t h, int64_t w, int exact, int64_t i, int64_t j,
+                                          const smo_hyper &hp, float &mean, float &sq_mean) {
+    int64_t r0, r1, c0, c1;
+    if (exact) {
+        int64_t kh = H / h, kw = W / w;
+        r0 = i * kh; r1 = r0 + kh;
+        c0 = j * kw; c1 = c0 + kw;
+    } else {
+        r0 = (i * H) / h; r1 = ((i + 1) * H + h - 1) / h;
+        c0 = (j * W) / w; c1 = ((j + 1) * W + w - 1) / w;
+    }
+    float s1 = 0.0f, s2 = 0.0f;
+    for (int64_t r = r0; r < r1; r++) {
+        const float *gr = g + r * W, *pr = p + r * W;
+        for (int64_t c = c0; c < c1; c++) {
+            float x = decayed(gr[c], pr[c], hp);
+            s1 = __fadd_rn(s1, x);
+            s2 = __fadd_rn(s2, __fmul_rn(x, x));
+        }
+    }
+    if (exact) {
+        float div = (float)((r1 - r0) * (c1 - c0));
+        mean = __fdiv_rn(s1, div);
+        sq_mean = __fdiv_rn(s2, div);
+    } else {
+        float dh = (float)(r1 - r0), dw = (float)(c1 - c0);
+        mean = __fdiv_rn(__fdiv_rn(s1, dh), dw);
+        sq_mean = __fdiv_rn(__fdiv_rn(s2, dh), dw);
+    }
+}
+
+}  // namespace smo

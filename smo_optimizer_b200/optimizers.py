@@ -1,0 +1,413 @@
+"""Drop-in ``SMO8bit`` and ``SMO`` optimizers running the step on the B200.
+
+Same constructor arguments, errors, per-group ``compress`` contract and
+``state_dict`` layout as the reference classes
+(smo/optimizers/spatial_8bit.py:27-374, smo/optimizers/spatial.py:35-208);
+the per-tensor arithmetic runs in the CUDA library (include/smo_b200.h), one
+``smo_step`` call per device per step, on the current CUDA stream.
+
+Differences a user can observe:
+  * Tensors must live on a CUDA device and be fp32; there is no CPU path.
+  * Pooled moments are double-buffered: after a step ``state[p]['m_q']`` (and
+    the other moment tensors) refer to the buffer the step wrote, and the
+    previous buffer is reused two steps later.  ``state_dict()`` returns live
+    references (as torch.optim.Adam does); deep-copy a snapshot to keep it.
+  * ``SMO`` needs no full-resolution reconstruction buffers: the kernels
+    reconstruct the moments in registers.  ``_param_buffers`` stays empty.
+  * Extra constructor arguments: ``k`` (alias of ``k_ratio``) and
+    ``protect_output`` (the grouping rule of the reference's benchmark
+    harness, which needs named parameters).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+from torch.optim.optimizer import Optimizer
+
+from . import _host, _lib
+
+__all__ = ["SMO", "SMO8bit", "protected_param_groups"]
+
+
+def protected_param_groups(named_params, protect_output, quant_capable: bool = True):
+    """Param groups of the reference harness's ``protect_output`` rule.
+
+    benchmarks/suites/comparison/t4_memory_benchmark.py:117-133: parameters
+    whose name contains ``"emb"`` or ``"head"`` are protected: dense fp32
+    moments (``True`` / ``"dense"``) or full-resolution int8 moments
+    (``"quant"``, SMO8bit only; SMO falls back to dense).
+    """
+    named_params = list(named_params)
+    if not protect_output:
+        return [{"params": [p for _, p in named_params]}]
+    mode = protect_output if protect_output in ("dense", "quant") else "dense"
+    if mode == "quant" and not quant_capable:
+        mode = "dense"
+    flag = "quant_only" if mode == "quant" else False
+    protected, regular = [], []
+    for name, p in named_params:
+        (protected if ("emb" in name or "head" in name) else regular).append(p)
+    groups = []
+    if regular:
+        groups.append({"params": regular, "compress": True})
+    if protected:
+        groups.append({"params": protected, "compress": flag})
+    return groups
+
+
+def _named(params):
+    params = list(params)
+    if params and isinstance(params[0], tuple) and len(params[0]) == 2 and isinstance(params[0][0], str):
+        return params
+    raise ValueError("protect_output needs named parameters: pass model.named_parameters()")
+
+
+class _Plan:
+    """Cached descriptor table of one device's tensors (rebuilt when the set changes)."""
+
+    def __init__(self, key, table):
+        self.key = key
+        self.table = table
+
+
+class _SpatialBase(Optimizer):
+    _name = "SMO"
+    _quant = False
+
+    def __init__(self, params, defaults, compress_conv, protect_output):
+        if protect_output:
+            params = protected_param_groups(_named(params), protect_output, quant_capable=self._quant)
+        super().__init__(params, defaults)
+        self.compress_conv = bool(compress_conv)
+        self._spare = {}        # param -> alternate moment buffers (double buffering)
+        self._workspace = {}    # device index -> uint8 workspace tensor
+        self._hyper_cache = {}
+
+    # ---------------------------------------------------------------- state
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        self._spare.clear()
+
+    def _hyper(self, group, step):
+        betas = group["betas"]
+        key = (group["lr"], betas[0], betas[1], group["eps"], group["weight_decay"], step)
+        hp = self._hyper_cache.get(key)
+        if hp is None:
+            s = _host.step_scalars(group["lr"], betas, group["eps"], group["weight_decay"], step)
+            hp = (s.beta1, s.omb1, s.beta2, s.omb2, s.wd, s.wd_on, s.neg_step, s.sqrt_bc2, s.eps, 0)
+            if len(self._hyper_cache) > 4096:
+                self._hyper_cache.clear()
+            self._hyper_cache[key] = hp
+        return hp
+
+    def _init_state(self, p, grad, group):
+        raise NotImplementedError
+
+    def _fill(self, rec, p, grad, state, group):
+        raise NotImplementedError
+
+    # ---------------------------------------------------------------- step
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+
+        per_dev = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if p.grad is None:
+                    continue
+                grad = p.grad
+                if grad.is_sparse:
+                    raise RuntimeError(f"{self._name} does not support sparse gradients.")
+                self._check_compress(group)
+                if p.device.type != "cuda":
+                    raise RuntimeError(f"{self._name} (B200 build) steps CUDA tensors only; "
+                                       f"got a parameter on {p.device}")
+                if p.dtype != torch.float32 or grad.dtype != torch.float32:
+                    raise TypeError(f"{self._name} (B200 build) supports fp32 parameters and gradients; "
+                                    f"got {p.dtype} / {grad.dtype}")
+                state = self.state[p]
+                if len(state) == 0:
+                    self._init_state(p, grad, group)
+                state["step"] += 1
+                per_dev.setdefault(p.device, []).append((p, grad, state, group))
+
+        for dev, items in per_dev.items():
+            self._launch(dev, items)
+        return loss
+
+    def _check_compress(self, group):
+        pass
+
+    def _launch(self, dev, items):
+        table = np.zeros(len(items), dtype=_lib.TENSOR_DTYPE)
+        keep = []
+        for i, (p, grad, state, group) in enumerate(items):
+            if not grad.is_contiguous():
+                grad = grad.contiguous()
+                keep.append(grad)
+            self._fill(table[i], p, grad, state, group)
+        with torch.cuda.device(dev):
+            nbytes = _lib.workspace_size(table)
+            ws = self._workspace.get(dev.index)
+            if ws is None or ws.numel() < nbytes:
+                ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+                self._workspace[dev.index] = ws
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _lib.step(table, ws.data_ptr(), ws.numel(), stream)
+        for p, grad, state, group in items:
+            self._swap(p, state)
+
+    def _swap(self, p, state):
+        pass
+
+    def workspace_status(self) -> int:
+        """Device-side status of the last step on each device (synchronises)."""
+        worst = 0
+        lib = _lib.load()
+        for idx, ws in self._workspace.items():
+            with torch.cuda.device(idx):
+                st = lib.smo_workspace_status(ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
+            worst = worst or st
+        return worst
+
+
+class SMO8bit(_SpatialBase):
+    """SMO-8bit: spatially pooled, block-wise int8 moments (spatial_8bit.py:27-79).
+
+    Args are those of the reference; ``k`` is an alias of ``k_ratio`` and
+    ``protect_output`` builds the reference harness's param groups.
+    """
+    _name = "SMO8bit"
+    _quant = True
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0, k_ratio=0.25,
+                 block_size=64, low_peak=False, band_mb=64.0, permute_basis=False, compress_conv=False,
+                 k=None, protect_output=False):
+        if k is not None:
+            k_ratio = k
+        if not 0.0 <= lr:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if not 0.0 <= eps:
+            raise ValueError(f"Invalid epsilon value: {eps}")
+        if not 0.0 <= betas[0] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 0: {betas[0]}")
+        if not 0.0 <= betas[1] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
+        if not 0.0 < k_ratio <= 1.0:
+            raise ValueError(f"Invalid k_ratio: {k_ratio}")
+        if block_size <= 0:
+            raise ValueError(f"Invalid block_size: {block_size}")
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, k_ratio=k_ratio,
+                        block_size=block_size)
+        super().__init__(params, defaults, compress_conv, protect_output)
+        self.low_peak = low_peak
+        self.band_mb = float(band_mb)
+        if low_peak and permute_basis:
+            raise ValueError("permute_basis is not supported with low_peak")
+        if permute_basis:
+            raise NotImplementedError("permute_basis (the basis-permutation ablation) is not implemented "
+                                      "in the B200 build")
+        self.permute_basis = permute_basis
+
+    # reference helpers (spatial_8bit.py:81-122), on CUDA tensors
+    @staticmethod
+    def _compress_2d(tensor, target_shape):
+        from . import ops
+        return ops.compress_2d(tensor, target_shape)
+
+    def _quantize_blockwise(self, data, block_size):
+        from . import ops
+        q, s = ops.quantize_blockwise(data, block_size)
+        return q, s, data.shape
+
+    def _dequantize_blockwise(self, q_blocks, scales, orig_shape, numel=None, dtype=None):
+        from . import ops
+        if numel is None:
+            numel = math.prod(orig_shape)
+        out = ops.dequantize_blockwise(q_blocks, scales, numel, q_blocks.shape[-1])
+        if dtype is not None:
+            out = out.to(dtype)
+        return out.view(orig_shape)
+
+    def _check_compress(self, group):
+        pass
+
+    def _init_state(self, p, grad, group):
+        state = self.state[p]
+        state["step"] = 0
+        raw = group.get("compress", True)
+        dev = grad.device
+        if raw == "quant_only":
+            state["is_quant_only"] = True
+            state["is_compressed"] = False
+            state["q_shape"] = tuple(grad.shape)
+            state["q_numel"] = grad.numel()
+            qb = _host.quant_only_q_block(grad.shape, group["block_size"])
+            state["q_block"] = qb
+            nb = _host.num_blocks(grad.numel(), qb)
+            state["m_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
+            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["v_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
+            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            return
+        view = _host.compression_view(grad.shape, self.compress_conv) if raw else None
+        if view is not None and p.is_contiguous():
+            vshape, pshape = view
+            state["is_compressed"] = True
+            state["orig_shape"] = vshape
+            state["param_shape"] = pshape
+            cs = _host.comp_shape(vshape, group["k_ratio"])
+            state["comp_numel"] = cs[0] * cs[1]
+            qb = _host.pooled_q_block(pshape, cs, group["block_size"])
+            state["q_block"] = qb
+            nb = _host.num_blocks(cs[0] * cs[1], qb)
+            # quantising zeros gives zero codes and 1e-12 scales (spatial_8bit.py:195-200)
+            state["m_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
+            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["v_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
+            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["comp_shape"] = cs
+        else:
+            state["is_compressed"] = False
+            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+
+    def _spares(self, p, state):
+        sp = self._spare.get(p)
+        if sp is None or sp[0].shape != state["m_q"].shape:
+            sp = tuple(torch.empty_like(state[k]) for k in ("m_q", "m_s", "v_q", "v_s"))
+            self._spare[p] = sp
+        return sp
+
+    def _fill(self, rec, p, grad, state, group):
+        rec["param"] = p.data_ptr()
+        rec["grad"] = grad.data_ptr()
+        rec["hp"] = self._hyper(group, state["step"])
+        if state.get("is_quant_only"):
+            rec["kind"] = _lib.SMO_KIND_QUANT_ONLY
+            rec["rows"], rec["cols"] = p.numel(), 1
+            rec["q_block"] = state["q_block"]
+            for k in ("m_q", "m_s", "v_q", "v_s"):
+                rec[k + "_in"] = rec[k + "_out"] = state[k].data_ptr()
+        elif state["is_compressed"]:
+            if not p.is_contiguous():
+                raise RuntimeError("a pooled parameter must stay contiguous (it was at init)")
+            rec["kind"] = _lib.SMO_KIND_POOLED8
+            rec["rows"], rec["cols"] = state["orig_shape"]
+            rec["comp_rows"], rec["comp_cols"] = state["comp_shape"]
+            rec["q_block"] = state["q_block"]
+            if self.low_peak and _host.can_band(state["orig_shape"], state["comp_shape"]):
+                rec["interp_band"] = _host.band_comp_rows(state["orig_shape"], state["comp_shape"],
+                                                          self.band_mb, grad.element_size())
+            sp = self._spares(p, state)
+            for k, s in zip(("m_q", "m_s", "v_q", "v_s"), sp):
+                rec[k + "_in"] = state[k].data_ptr()
+                rec[k + "_out"] = s.data_ptr()
+        else:
+            if not p.is_contiguous():
+                raise NotImplementedError("non-contiguous dense parameters are not supported")
+            rec["kind"] = _lib.SMO_KIND_DENSE
+            rec["rows"], rec["cols"] = p.numel(), 1
+            rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()
+            rec["v_in"] = rec["v_out"] = state["exp_avg_sq"].data_ptr()
+
+    def _swap(self, p, state):
+        if state.get("is_compressed"):
+            sp = self._spare[p]
+            old = tuple(state[k] for k in ("m_q", "m_s", "v_q", "v_s"))
+            for k, s in zip(("m_q", "m_s", "v_q", "v_s"), sp):
+                state[k] = s
+            self._spare[p] = old
+
+
+class SMO(_SpatialBase):
+    """SMO-Spatial: spatially pooled fp32 moments (spatial.py:35-75)."""
+    _name = "SMO"
+    _quant = False
+
+    def __init__(self, params, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0, k_ratio=0.25,
+                 compress_conv=False, k=None, protect_output=False):
+        if k is not None:
+            k_ratio = k
+        if not 0.0 <= lr:
+            raise ValueError(f"Invalid learning rate: {lr}")
+        if not 0.0 <= eps:
+            raise ValueError(f"Invalid epsilon value: {eps}")
+        if not 0.0 <= betas[0] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 0: {betas[0]}")
+        if not 0.0 <= betas[1] < 1.0:
+            raise ValueError(f"Invalid beta parameter at index 1: {betas[1]}")
+        if not 0.0 < k_ratio <= 1.0:
+            raise ValueError(f"Invalid k_ratio: {k_ratio}. Must be in (0, 1]")
+        defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, k_ratio=k_ratio)
+        super().__init__(params, defaults, compress_conv, protect_output)
+        # The reference caches full-resolution reconstruction buffers here
+        # (spatial.py:73-75); the fused kernels need none, so it stays empty.
+        self._param_buffers = {}
+
+    @staticmethod
+    def _compress_2d(tensor, target_shape):
+        from . import ops
+        return ops.compress_2d(tensor, target_shape)
+
+    def _check_compress(self, group):
+        if group.get("compress", True) == "quant_only":
+            raise ValueError("SMO (fp32) has no int8 storage; 'quant_only' groups require SMO8bit")
+
+    def _init_state(self, p, grad, group):
+        state = self.state[p]
+        state["step"] = 0
+        use = group.get("compress", True)
+        view = _host.compression_view(grad.shape, self.compress_conv) if use else None
+        if view is not None and p.is_contiguous():
+            vshape, pshape = view
+            state["is_compressed"] = True
+            cs = _host.comp_shape(vshape, group["k_ratio"])
+            state["exp_avg"] = torch.zeros(cs, dtype=grad.dtype, device=grad.device)
+            state["exp_avg_sq"] = torch.zeros(cs, dtype=grad.dtype, device=grad.device)
+            state["orig_shape"] = vshape
+            state["param_shape"] = pshape
+        else:
+            state["is_compressed"] = False
+            state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+
+    def _fill(self, rec, p, grad, state, group):
+        rec["param"] = p.data_ptr()
+        rec["grad"] = grad.data_ptr()
+        rec["hp"] = self._hyper(group, state["step"])
+        if state["is_compressed"]:
+            if not p.is_contiguous():
+                raise RuntimeError("a pooled parameter must stay contiguous (it was at init)")
+            rec["kind"] = _lib.SMO_KIND_POOLED32
+            rec["rows"], rec["cols"] = state["orig_shape"]
+            rec["comp_rows"], rec["comp_cols"] = state["exp_avg"].shape
+            sp = self._spare.get(p)
+            if sp is None or sp[0].shape != state["exp_avg"].shape:
+                sp = (torch.empty_like(state["exp_avg"]), torch.empty_like(state["exp_avg_sq"]))
+                self._spare[p] = sp
+            rec["m_in"], rec["v_in"] = state["exp_avg"].data_ptr(), state["exp_avg_sq"].data_ptr()
+            rec["m_out"], rec["v_out"] = sp[0].data_ptr(), sp[1].data_ptr()
+        else:
+            if not p.is_contiguous():
+                raise NotImplementedError("non-contiguous dense parameters are not supported")
+            rec["kind"] = _lib.SMO_KIND_DENSE
+            rec["rows"], rec["cols"] = p.numel(), 1
+            rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()
+            rec["v_in"] = rec["v_out"] = state["exp_avg_sq"].data_ptr()
+
+    def _swap(self, p, state):
+        if state.get("is_compressed"):
+            sp = self._spare[p]
+            old = (state["exp_avg"], state["exp_avg_sq"])
+            state["exp_avg"], state["exp_avg_sq"] = sp
+            self._spare[p] = old

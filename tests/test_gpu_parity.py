@@ -1,0 +1,180 @@
+"""GPU parity: the CUDA library against the CPU oracle and the reference goldens.
+
+Everything here calls the library through its C ABI (directly via ctypes, or
+through the drop-in optimizer classes that bind it).
+
+Expected agreement:
+  * with the oracle: bit-identical codes, scales, moments and params (both
+    sides round every fp32 operation the same way, IEEE sqrt included);
+  * with the reference (golden files): codes bit-identical except <= 1e-5 of
+    them by one LSB, scales and params within rtol 1e-5 / atol 1e-7.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from _golden import code_mismatch_fraction, load
+from oracle import oracle
+from smo_optimizer_b200 import SMO, SMO8bit, _host, _lib, ops, synthetic
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-7
+CODE_FRAC = 1e-5
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.fail("no CUDA device: GPU tests need a B200")
+    _lib.load()
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    return t.detach().cpu().numpy()
+
+
+# ------------------------------------------------------------------ stages
+
+def test_synth_normal_matches_host_generator():
+    for n, off in [(1, 0), (1000, 0), (12345, 77), (1 << 20, 3)]:
+        ref = synthetic.synth_normal(7, 99, n, 1e-3, offset=off)
+        t = torch.empty(n, dtype=torch.float32, device="cuda")
+        ops.synth_normal_(t, 7, 99, 1e-3, offset=off)
+        assert np.array_equal(host(t).view(np.uint32), ref.view(np.uint32))
+
+
+@pytest.mark.parametrize("n,block", [(65536, 64), (84, 64), (100, 18), (453, 64), (7, 1), (4096, 256)])
+def test_quantize_dequantize_match_oracle(n, block):
+    rng = np.random.default_rng(n + block)
+    x = (rng.standard_normal(n) * 1e-3).astype(np.float32)
+    x[::17] = 0.0
+    q_ref, s_ref = oracle.quantize(x, block)
+    q, s = ops.quantize_blockwise(cuda(x), block)
+    assert np.array_equal(host(q), q_ref)
+    assert np.array_equal(host(s), s_ref)
+    d_ref = oracle.dequantize(q_ref, s_ref, n, block)
+    d = ops.dequantize_blockwise(q, s, n, block)
+    assert np.array_equal(host(d), d_ref)
+
+
+@pytest.mark.parametrize("H,W,h,w,wd", [(1024, 1024, 256, 256, 0.01), (64, 64, 16, 16, 0.0), (50, 30, 12, 7, 0.01),
+                                        (100, 200, 30, 60, 0.01), (33, 65, 8, 16, 0.0), (96, 96, 32, 32, 0.01)])
+def test_pool_pair_matches_oracle(H, W, h, w, wd):
+    g = synthetic.synth_normal(1, 1, H * W, 1e-3).reshape(H, W)
+    p = synthetic.synth_normal(1, 2, H * W, 0.02).reshape(H, W)
+    sc = _host.step_scalars(1e-3, (0.9, 0.999), 1e-8, wd, 1)
+    ref_m, ref_2 = oracle.pool_pair(g, p, (h, w), sc)
+    om, o2 = ops.pool2d_pair(cuda(g), (h, w), cuda(p), wd)
+    assert np.array_equal(host(om), ref_m)
+    assert np.array_equal(host(o2), ref_2)
+
+
+@pytest.mark.parametrize("h,w,H,W,band", [(256, 256, 1024, 1024, 0), (16, 16, 64, 64, 0), (12, 7, 50, 30, 0),
+                                          (30, 60, 100, 200, 0), (32, 64, 128, 256, 12), (202, 24, 808, 96, 3),
+                                          (16, 16, 48, 48, 2), (64, 64, 64, 64, 0)])
+def test_upsample_matches_oracle(h, w, H, W, band):
+    src = synthetic.synth_normal(3, 5, h * w, 1.0).reshape(h, w)
+    ref = oracle.upsample(src, (H, W), band)
+    out = ops.upsample2d(cuda(src), (H, W), band)
+    assert np.array_equal(host(out), ref)
+
+
+def test_bounded_wait_times_out_and_context_survives():
+    lib = _lib.load()
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    import ctypes
+    st = ctypes.c_int32(-1)
+    _lib.check(lib.smo_selftest_wait_timeout(ws.data_ptr(), ws.numel(), 2000, ctypes.byref(st),
+                                             torch.cuda.current_stream().cuda_stream), "selftest")
+    assert st.value == _lib.SMO_ERR_TIMEOUT
+    # the context is still usable
+    x = torch.ones(1000, device="cuda")
+    assert float(x.sum().item()) == 1000.0
+
+
+# ------------------------------------------------------------------ full steps
+
+def run_gpu_case(name, steps=None):
+    case = C.CASES[name]
+    params = [torch.nn.Parameter(cuda(a)) for a in C.case_params(case)]
+    groups = C.case_groups(case, params)
+    cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
+    opt = cls(groups, **case["kwargs"])
+    for step in range(1, (steps or case["steps"]) + 1):
+        for p, g in zip(params, C.case_grads(case, step)):
+            p.grad = cuda(g)
+        opt.step()
+    torch.cuda.synchronize()
+    return params, [opt.state[p] for p in params]
+
+
+def run_oracle_case(name, steps=None):
+    case = C.CASES[name]
+    params = C.case_params(case)
+    groups = C.case_groups(case, params)
+    opt = oracle.OracleOptimizer(case["opt"], groups, **case["kwargs"])
+    keys = [k for k, _, _ in opt.params()]
+    for step in range(1, (steps or case["steps"]) + 1):
+        opt.step(C.case_grads(case, step))
+    return params, [opt.state[k] for k in keys]
+
+
+ALL_CASES = [n for n in C.CASES if n != "single1024"]
+
+
+@pytest.mark.parametrize("name", ALL_CASES)
+def test_step_bit_exact_vs_oracle(name):
+    gp, gs = run_gpu_case(name)
+    op, os_ = run_oracle_case(name)
+    for i, (p, st, ref_p, ref_st) in enumerate(zip(gp, gs, op, os_)):
+        for k in C.STATE_ARRAY_KEYS:
+            if k in ref_st:
+                got = host(st[k]).reshape(-1)
+                ref = np.asarray(ref_st[k]).reshape(-1)
+                assert np.array_equal(got, ref), f"{name}[{i}] {k} differs from the oracle"
+        assert np.array_equal(host(p).reshape(-1), ref_p.reshape(-1)), f"{name}[{i}] param differs from the oracle"
+
+
+@pytest.mark.parametrize("name", ALL_CASES + ["single1024"])
+def test_step_matches_reference_goldens(name):
+    gp, gs = run_gpu_case(name)
+    case = C.CASES[name]
+    gold, meta = load(name)
+    stride = case.get("sample_stride")
+    for i, (p, st) in enumerate(zip(gp, gs)):
+        for k, v in meta["tensors"][i].items():
+            got = st.get(k)
+            got = list(got) if isinstance(got, tuple) else got
+            assert got == v, f"{name}[{i}] state[{k!r}]"
+        for k in C.STATE_ARRAY_KEYS:
+            gk = f"{i}.{k}"
+            assert (gk in gold) == (k in st)
+            if gk not in gold:
+                continue
+            ref = gold[gk]
+            got = host(st[k]).reshape(ref.shape)
+            if ref.dtype == np.int8:
+                assert code_mismatch_fraction(got, ref) <= CODE_FRAC
+            else:
+                np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
+        flat = host(p).reshape(-1)
+        if stride:
+            np.testing.assert_allclose(flat[C.sample_indices(flat.size, stride)], gold[f"{i}.param_sample"],
+                                       rtol=RTOL, atol=ATOL)
+        else:
+            np.testing.assert_allclose(flat, gold[f"{i}.param"], rtol=RTOL, atol=ATOL)
+
+
+def test_single1024_100_steps_bit_exact_vs_oracle():
+    gp, gs = run_gpu_case("single1024")
+    op, os_ = run_oracle_case("single1024")
+    for k in ("m_q", "m_s", "v_q", "v_s"):
+        assert np.array_equal(host(gs[0][k]).reshape(-1), np.asarray(os_[0][k]).reshape(-1)), k
+    assert np.array_equal(host(gp[0]).reshape(-1), op[0].reshape(-1))

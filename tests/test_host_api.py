@@ -1,0 +1,170 @@
+"""CPU-only checks: the C ABI library loads and exports what the header
+declares, the ctypes layout matches the C struct, the host-side shape rules
+match the reference's state metadata, and the drop-in classes keep the
+reference's constructor/step errors (tests/test_spatial_optimizers.py:50-58,
+:269-274, :400-402 of the reference)."""
+
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+import cases as C
+from _golden import load
+from smo_optimizer_b200 import SMO, SMO8bit, _host, _lib, compression_view, protected_param_groups
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "smo_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"SMO_API\s+[\w\s\*]+?\b(smo_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.lib_path())
+    names = declared_functions()
+    assert len(names) >= 12
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in smo_b200.h but not exported"
+
+
+def test_binding_layout_matches_library():
+    lib = _lib.load()
+    assert lib.smo_abi_version() == _lib.ABI_VERSION
+    assert lib.smo_tensor_struct_size() == _lib.TENSOR_DTYPE.itemsize == 208
+
+
+def test_status_strings_and_host_side_validation():
+    lib = _lib.load()
+    assert lib.smo_status_string(0) == b"ok"
+    assert lib.smo_status_string(5).startswith(b"bounded")
+    # descriptors are validated before anything is launched (no GPU needed)
+    t = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    t["kind"] = 99
+    t["param"] = t["grad"] = 256
+    ws = (ctypes.c_uint8 * 4096)()
+    addr = (ctypes.addressof(ws) + 255) // 256 * 256
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 1           # SMO_ERR_INVALID
+    t["kind"] = _lib.SMO_KIND_DENSE
+    t["cols"] = 1
+    t["param"] = 258                                                          # misaligned fp32 pointer
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 2           # SMO_ERR_ALIGNMENT
+    t["param"] = 256
+    assert lib.smo_step(t.ctypes.data, 1, None, 0, None) == 1              # dense: no pointers for m/v
+    assert lib.smo_step(t.ctypes.data, 0, addr, 2048, None) == 0           # empty step is a no-op
+
+
+@pytest.mark.parametrize("name", list(C.CASES))
+def test_host_rules_match_reference_metadata(name):
+    """compression_view / comp_shape / q_block / quant_only layout agree with the
+    state metadata the reference produced for each golden case."""
+    case = C.CASES[name]
+    _, meta = load(name)
+    kw = case["kwargs"]
+    specs = case.get("groups") or [{}]
+    for i, ((shape, gi), tm) in enumerate(zip(case["tensors"], meta["tensors"])):
+        raw = specs[gi].get("compress", True)
+        if raw == "quant_only":
+            assert tm["is_quant_only"] and tm["q_block"] == _host.quant_only_q_block(shape, kw.get("block_size", 64))
+            continue
+        view = compression_view(shape, kw.get("compress_conv", False)) if raw else None
+        assert tm["is_compressed"] == (view is not None)
+        if view is None:
+            continue
+        vshape, pshape = view
+        assert tm["orig_shape"] == list(vshape) and tm["param_shape"] == list(pshape)
+        cs = _host.comp_shape(vshape, kw["k_ratio"])
+        if case["opt"] == "SMO8bit":
+            assert tm["comp_shape"] == list(cs)
+            assert tm["q_block"] == _host.pooled_q_block(pshape, cs, kw.get("block_size", 64))
+
+
+def test_compression_view_rules():
+    # reference tests/test_spatial_optimizers.py:119-130
+    assert compression_view((64, 64)) == ((64, 64), (64, 64))
+    assert compression_view((16, 16)) is None
+    assert compression_view((256, 128, 3, 3)) is None
+    assert compression_view((256, 128, 3, 3), include_conv=True) == ((256, 1152), (256, 128, 3, 3))
+    assert compression_view((16, 3, 3, 3), include_conv=True) is None
+    assert compression_view((8, 16, 32), include_conv=True) is None
+
+
+def test_band_rows_formula():
+    # spatial_8bit.py:359 with band_mb = 0.05 on a (128, 256) view at k=0.25
+    assert _host.band_comp_rows((128, 256), (32, 64), 0.05) == max(2, int(0.05 * 1024 ** 2 / (2 * 256 * 4 * 4)))
+    assert _host.band_comp_rows((1536, 6144), (384, 1536), 64.0) == 341
+
+
+def test_step_scalars_follow_python_double_arithmetic():
+    s = _host.step_scalars(1e-3, (0.9, 0.999), 1e-8, 0.01, 3)
+    assert s.neg_step == np.float32(-(1e-3 / (1 - 0.9 ** 3)))
+    assert s.sqrt_bc2 == np.float32((1 - 0.999 ** 3) ** 0.5)
+    assert s.omb1 == np.float32(1 - 0.9) and s.wd_on == 1
+    assert _host.step_scalars(1e-3, (0.9, 0.999), 1e-8, 0, 1).wd_on == 0
+
+
+@pytest.mark.parametrize("cls", [SMO, SMO8bit])
+def test_constructor_errors(cls):
+    p = [torch.nn.Parameter(torch.zeros(32, 32))]
+    for kw in (dict(lr=-1.0), dict(eps=-1.0), dict(betas=(1.0, 0.9)), dict(betas=(0.9, 1.0)), dict(k_ratio=0.0),
+               dict(k_ratio=1.5)):
+        with pytest.raises(ValueError):
+            cls(p, **kw)
+    if cls is SMO8bit:
+        with pytest.raises(ValueError):
+            cls(p, block_size=0)
+        with pytest.raises(ValueError):
+            cls(p, low_peak=True, permute_basis=True)
+
+
+def test_k_alias_and_defaults():
+    p = [torch.nn.Parameter(torch.zeros(32, 32))]
+    opt = SMO8bit(p, k=0.5)
+    g = opt.param_groups[0]
+    assert g["k_ratio"] == 0.5 and g["block_size"] == 64 and g["lr"] == 1e-3
+    assert SMO(p).param_groups[0]["k_ratio"] == 0.25
+    assert SMO(p)._param_buffers == {}
+
+
+def test_sparse_gradient_rejected():
+    dense = torch.nn.Parameter(torch.zeros(8, 8))
+    opt = SMO8bit([dense], lr=1e-3)
+    dense.grad = torch.sparse_coo_tensor(torch.tensor([[0, 1], [2, 3]]), torch.tensor([1.0, -1.0]), dense.shape)
+    with pytest.raises(RuntimeError):
+        opt.step()
+
+
+def test_smo_rejects_quant_only_group():
+    p = torch.nn.Parameter(torch.zeros(64, 64))
+    opt = SMO([{"params": [p], "compress": "quant_only"}], lr=1e-3)
+    p.grad = torch.randn_like(p)
+    with pytest.raises(ValueError):
+        opt.step()
+
+
+def test_cpu_tensors_fail_loudly():
+    p = torch.nn.Parameter(torch.zeros(64, 64))
+    opt = SMO8bit([p])
+    p.grad = torch.zeros_like(p)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        opt.step()
+
+
+def test_protect_output_groups():
+    named = [("tok_emb.weight", torch.nn.Parameter(torch.zeros(4, 4))),
+             ("blocks.0.attn.in_proj_weight", torch.nn.Parameter(torch.zeros(4, 4))),
+             ("head.weight", torch.nn.Parameter(torch.zeros(4, 4)))]
+    groups = protected_param_groups(named, True)
+    assert [len(g["params"]) for g in groups] == [1, 2]
+    assert groups[0]["compress"] is True and groups[1]["compress"] is False
+    assert protected_param_groups(named, "quant")[1]["compress"] == "quant_only"
+    assert protected_param_groups(named, "quant", quant_capable=False)[1]["compress"] is False
+    opt = SMO8bit(named, protect_output="dense")
+    assert len(opt.param_groups) == 2 and opt.param_groups[1]["compress"] is False
+    with pytest.raises(ValueError):
+        SMO8bit([p for _, p in named], protect_output=True)
