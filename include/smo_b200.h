@@ -49,6 +49,10 @@ typedef enum smo_kind {
     SMO_KIND_QUANT_ONLY = 4  /* full-resolution int8 moments (spatial_8bit.py:157-169) */
 } smo_kind;
 
+/* smo_tensor.flags */
+#define SMO_FLAG_GENERAL_PATH 1  /* step this tensor with the general two-launch kernels
+                                    even when the fused single-pass kernel could take it */
+
 /* fp32 scalars of one tensor's step.  The host forms each in double exactly as
  * the reference's Python does (spatial_8bit.py:210-297) and rounds once. */
 typedef struct smo_hyper {
@@ -63,7 +67,9 @@ typedef struct smo_hyper {
 } smo_hyper;
 
 /* One parameter tensor of a step.  Moments are read from *_in and written to
- * *_out; in == out is allowed.  Fields a kind does not use must be NULL / 0.
+ * *_out.  in == out is allowed, but pooled tensors then take the general
+ * two-launch kernels (the fused single-pass kernel needs separate buffers).
+ * Fields a kind does not use must be NULL / 0.
  *
  *   POOLED8    param/grad [rows*cols]; codes [ceil(C/q_block)*q_block] int8,
  *              scales [ceil(C/q_block)] fp32, C = comp_rows*comp_cols
@@ -92,7 +98,7 @@ typedef struct smo_tensor {
     int64_t interp_band;            /* low_peak: compact rows per interpolation band
                                        (spatial_8bit.py:359); 0 = monolithic */
     int32_t kind;                   /* smo_kind */
-    int32_t flags;                  /* reserved, 0 */
+    int32_t flags;                  /* SMO_FLAG_* (0 = let the library choose the kernel) */
     smo_hyper hp;
 } smo_tensor;
 

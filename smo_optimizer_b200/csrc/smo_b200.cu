@@ -376,7 +376,7 @@ static inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; 
 
 // scratch bytes of the general path for one tensor (POOLED8 post-EMA moments)
 static inline size_t general_scratch(const smo_tensor &t) {
-    if (t.kind != SMO_KIND_POOLED8) return 0;
+    if (t.kind != SMO_KIND_POOLED8 || fused_takes(t)) return 0;
     return 2 * round_up((size_t)t.comp_rows * (size_t)t.comp_cols * sizeof(float), kScratchAlign);
 }
 

@@ -85,6 +85,9 @@ class _SpatialBase(Optimizer):
         self._spare = {}        # param -> alternate moment buffers (double buffering)
         self._workspace = {}    # device index -> uint8 workspace tensor
         self._hyper_cache = {}
+        # smo_tensor.flags for every tensor (SMO_FLAG_GENERAL_PATH pins the
+        # general two-launch kernels; used to cross-check the fused kernel)
+        self._kernel_flags = 0
 
     # ---------------------------------------------------------------- state
 
@@ -291,6 +294,7 @@ class SMO8bit(_SpatialBase):
     def _fill(self, rec, p, grad, state, group):
         rec["param"] = p.data_ptr()
         rec["grad"] = grad.data_ptr()
+        rec["flags"] = self._kernel_flags
         rec["hp"] = self._hyper(group, state["step"])
         if state.get("is_quant_only"):
             rec["kind"] = _lib.SMO_KIND_QUANT_ONLY
@@ -384,6 +388,7 @@ class SMO(_SpatialBase):
     def _fill(self, rec, p, grad, state, group):
         rec["param"] = p.data_ptr()
         rec["grad"] = grad.data_ptr()
+        rec["flags"] = self._kernel_flags
         rec["hp"] = self._hyper(group, state["step"])
         if state["is_compressed"]:
             if not p.is_contiguous():

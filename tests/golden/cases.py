@@ -61,6 +61,13 @@ CASES = {
     "s8_808x96_band": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64,
                                                       low_peak=True, band_mb=0.02),
                            tensors=[((808, 96), 0)], steps=3, seed=12),
+    # fused-kernel shapes: strips of 16, 16 and 1 compact rows, wide rows, low_peak bands
+    "s8_132x2048_band": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64,
+                                                        low_peak=True, band_mb=0.2),
+                             tensors=[((132, 2048), 0)], steps=3, seed=18, sample_stride=3),
+    # 8x8 windows (k = 0.125)
+    "s8_256x512_k0125": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.125, block_size=64),
+                             tensors=[((256, 512), 0)], steps=3, seed=19),
     # SMO-Spatial fp32 pooled moments
     "smo_96x192_k05": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
                            tensors=[((96, 192), 0), ((192,), 0)], steps=5, seed=13),

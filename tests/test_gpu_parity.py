@@ -101,17 +101,20 @@ def test_bounded_wait_times_out_and_context_survives():
 
 # ------------------------------------------------------------------ full steps
 
-def run_gpu_case(name, steps=None):
+def run_gpu_case(name, steps=None, general=False):
     case = C.CASES[name]
     params = [torch.nn.Parameter(cuda(a)) for a in C.case_params(case)]
     groups = C.case_groups(case, params)
     cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
     opt = cls(groups, **case["kwargs"])
+    if general:
+        opt._kernel_flags = 1  # SMO_FLAG_GENERAL_PATH
     for step in range(1, (steps or case["steps"]) + 1):
         for p, g in zip(params, C.case_grads(case, step)):
             p.grad = cuda(g)
         opt.step()
     torch.cuda.synchronize()
+    assert opt.workspace_status() == 0, "device-side status reports a failure"
     return params, [opt.state[p] for p in params]
 
 
@@ -178,3 +181,49 @@ def test_single1024_100_steps_bit_exact_vs_oracle():
     for k in ("m_q", "m_s", "v_q", "v_s"):
         assert np.array_equal(host(gs[0][k]).reshape(-1), np.asarray(os_[0][k]).reshape(-1)), k
     assert np.array_equal(host(gp[0]).reshape(-1), op[0].reshape(-1))
+
+
+FUSED_CASES = ["single1024", "s8_128x256_mono", "s8_128x256_band", "s8_128x256_band_wd", "s8_multi",
+               "s8_132x2048_band", "s8_256x512_k0125", "smo_96x192_k05", "smo_groups"]
+
+
+@pytest.mark.parametrize("name", FUSED_CASES)
+def test_fused_kernel_matches_general_kernels(name):
+    """The fused single-pass kernel and the general two-launch kernels agree bit for bit."""
+    steps = 4 if name == "single1024" else None
+    fp, fs = run_gpu_case(name, steps=steps)
+    gp, gs = run_gpu_case(name, steps=steps, general=True)
+    for i, (a, b, sa, sb) in enumerate(zip(fp, gp, fs, gs)):
+        assert torch.equal(a, b), f"{name}[{i}] params differ between fused and general kernels"
+        for k in C.STATE_ARRAY_KEYS:
+            if k in sa:
+                assert torch.equal(sa[k], sb[k]), f"{name}[{i}] {k} differs between fused and general kernels"
+
+
+@pytest.mark.parametrize("H,W,k,block,band_mb,wd", [
+    (4 * 33, 4 * 300, 0.25, 64, 0.0, 0.01),     # w=300: blocks straddle rows; strips 16,16,1
+    (4 * 17, 4 * 1000, 0.25, 40, 0.5, 0.0),     # w=1000 > threads: several columns per thread
+    (2 * 50, 2 * 700, 0.5, 64, 0.0, 0.01),      # 2x2 windows
+    (8 * 21, 8 * 40, 0.125, 20, 0.0, 0.01),     # 8x8 windows, block 20
+    (32, 4 * 1024, 0.25, 64, 0.0, 0.01),        # one strip of 8 compact rows, 4 columns per thread
+])
+def test_fused_random_shapes_vs_oracle(H, W, k, block, band_mb, wd):
+    kw = dict(lr=2e-3, betas=(0.8, 0.99), eps=1e-8, weight_decay=wd, k_ratio=k, block_size=block)
+    if band_mb:
+        kw.update(low_peak=True, band_mb=band_mb)
+    p0 = synthetic.synth_normal(5, H, H * W, 0.02).reshape(H, W)
+    p = torch.nn.Parameter(cuda(p0))
+    opt = SMO8bit([p], **kw)
+    ref_p = p0.copy()
+    ref = oracle.OracleOptimizer("SMO8bit", [{"params": [ref_p]}], **kw)
+    for step in range(1, 4):
+        g = synthetic.synth_normal(6, step * 1000 + W, H * W, 1e-3).reshape(H, W)
+        p.grad = cuda(g)
+        opt.step()
+        ref.step([g])
+    torch.cuda.synchronize()
+    assert opt.workspace_status() == 0
+    st, rst = opt.state[p], ref.state[(0, 0)]
+    for key in ("m_q", "m_s", "v_q", "v_s"):
+        assert np.array_equal(host(st[key]).reshape(-1), rst[key].reshape(-1)), key
+    assert np.array_equal(host(p), ref_p)
