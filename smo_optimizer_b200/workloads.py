@@ -98,4 +98,8 @@ WORKLOADS = {
     # ~700M decoder, SMO8bit k=0.25 low_peak (row-banded)
     "decoder700m": Workload("decoder700m", _decoder700m_tensors(), "SMO8bit",
                             dict(_HP, k_ratio=0.25, block_size=64, low_peak=True)),
+    # the first 4 layers of the ~700M decoder (113M params, ~1.4 GB of params and
+    # grads: larger than L2, small enough for profiler captures)
+    "decoder700m_4layers": Workload("decoder700m_4layers", _decoder700m_tensors()[:16], "SMO8bit",
+                                    dict(_HP, k_ratio=0.25, block_size=64, low_peak=True)),
 }
