@@ -32,6 +32,7 @@
 //
 // The parameter rows read in phase 1 are read again in phase 2 one pipeline
 // step later; that second read is meant to hit L2.
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -41,10 +42,23 @@
 namespace smo {
 
 constexpr int kFusedThreads = 256;
-constexpr int kMaxFused = 112;
+constexpr int kMaxFusedCtasPerSm = 4;
+constexpr int kMaxFused = 104;
 constexpr int64_t kStripRows = 16;          // target compact rows per strip
-constexpr int64_t kMaxFusedCols = 4096;     // compact columns (shared memory: 48 B per column, 192 KB max)
+constexpr int64_t kMaxFusedCols = 8192;     // compact columns (shared memory: 24 B per column)
 constexpr int64_t kDefaultWaitIters = 1 << 22;
+
+// n / d for 32-bit unsigned n by a divisor fixed per tensor: multiply by a
+// precomputed magic number (Granlund-Montgomery / Hacker's Delight 10-1,
+// the round-up variant with a 33-bit add), set up on the host.
+struct FastDiv {
+    uint32_t d, m, l;
+};
+
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, const FastDiv &f) {
+    const uint32_t t = __umulhi(n, f.m);
+    return (uint32_t)(((uint64_t)t + n) >> f.l);
+}
 
 struct FusedDesc {
     float *p;
@@ -61,10 +75,11 @@ struct FusedDesc {
     const float *v_in;
     float *m_out;
     float *v_out;
-    int64_t H, W, h, w, B, band;
-    int64_t L;         // compact rows per strip
+    int64_t H, W, band;
     int64_t halo_off;  // float offset of this tensor's published rows in the halo area
-    float col_scale;   // (float)w / (float)W, correctly rounded
+    int32_t h, w, B, L;
+    FastDiv div_B;     // cell -> quant block
+    FastDiv div_w;     // cell -> compact row
     int32_t kind;
     smo_hyper hp;
 };
@@ -74,58 +89,50 @@ struct FusedBatch {
     int64_t strip_start[kMaxFused + 1];
     FusedDesc d[kMaxFused];
 };
-static_assert(sizeof(FusedBatch) < 32000, "kernel parameter batch must stay below 32 KB");
+static_assert(sizeof(FusedBatch) < 30000, "kernel parameter batch must stay below 32 KB");
 
 // ---------------------------------------------------------------- memory helpers
 
 template <int KW>
-__device__ __forceinline__ void load_row(const float *ptr, float (&v)[KW]) {
+__device__ __forceinline__ void load_grad_row(const float *ptr, float (&v)[KW]) {
     if constexpr (KW % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < KW / 4; k++) {
             float4 t = __ldcs(reinterpret_cast<const float4 *>(ptr) + k);
             v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
         }
-    } else if constexpr (KW == 2) {
+    } else {
+        static_assert(KW == 2, "window width");
         float2 t = __ldcs(reinterpret_cast<const float2 *>(ptr));
         v[0] = t.x; v[1] = t.y;
-    } else {
-#pragma unroll
-        for (int k = 0; k < KW; k++) v[k] = __ldcs(ptr + k);
     }
 }
 
-// parameter loads: default caching (phase 1, to be re-read) / last use (phase 2)
-template <int KW>
-__device__ __forceinline__ void load_param(const float *ptr, float (&v)[KW], bool last_use) {
+// parameter loads: L2-cached (phase 1, re-read one pipeline step later) or last use (phase 2)
+template <int KW, bool kLastUse>
+__device__ __forceinline__ void load_param_row(const float *ptr, float (&v)[KW]) {
     if constexpr (KW % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < KW / 4; k++) {
             const float4 *q = reinterpret_cast<const float4 *>(ptr) + k;
-            float4 t = last_use ? __ldlu(q) : __ldcg(q);
+            float4 t = kLastUse ? __ldlu(q) : __ldcg(q);
             v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
         }
-    } else if constexpr (KW == 2) {
-        const float2 *q = reinterpret_cast<const float2 *>(ptr);
-        float2 t = last_use ? __ldlu(q) : __ldcg(q);
-        v[0] = t.x; v[1] = t.y;
     } else {
-#pragma unroll
-        for (int k = 0; k < KW; k++) v[k] = last_use ? __ldlu(ptr + k) : __ldcg(ptr + k);
+        const float2 *q = reinterpret_cast<const float2 *>(ptr);
+        float2 t = kLastUse ? __ldlu(q) : __ldcg(q);
+        v[0] = t.x; v[1] = t.y;
     }
 }
 
 template <int KW>
-__device__ __forceinline__ void store_param(float *ptr, const float (&v)[KW]) {
+__device__ __forceinline__ void store_param_row(float *ptr, const float (&v)[KW]) {
     if constexpr (KW % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < KW / 4; k++)
             __stcs(reinterpret_cast<float4 *>(ptr) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
-    } else if constexpr (KW == 2) {
-        __stcs(reinterpret_cast<float2 *>(ptr), make_float2(v[0], v[1]));
     } else {
-#pragma unroll
-        for (int k = 0; k < KW; k++) __stcs(ptr + k, v[k]);
+        __stcs(reinterpret_cast<float2 *>(ptr), make_float2(v[0], v[1]));
     }
 }
 
@@ -149,87 +156,138 @@ __device__ __forceinline__ void report_error(WsHeader *hdr, unsigned int code, u
     if (atomicCAS(&hdr->error, 0u, code) == 0u) hdr->error_where = where;
 }
 
+// x / c for a per-tensor constant c with r = RN(1/c): Markstein's correction
+// (q0 = RN(x r), rem = x - q0 c exactly by fma, q = RN(q0 + rem r)) returns
+// the correctly rounded quotient for finite x away from under/overflow; here
+// x = sqrt(v) >= 0 and c = sqrt(1 - beta2^t) in (0, 1], so only x = +inf
+// needs the general division.
+__device__ __forceinline__ float div_by_const(float x, float c, float r) {
+    if (x == __int_as_float(0x7f800000)) return __fdiv_rn(x, c);
+    const float q0 = __fmul_rn(x, r);
+    const float rem = __fmaf_rn(-q0, c, x);
+    return __fmaf_rn(rem, r, q0);
+}
+
+__device__ __forceinline__ float adam_write_rc(float p, float m, float v, const smo_hyper &hp, float rcp_sbc2) {
+    const float d = __fadd_rn(div_by_const(__fsqrt_rn(v), hp.sqrt_bc2, rcp_sbc2), hp.eps);
+    return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
+}
+
 // ---------------------------------------------------------------- phases
+
+template <int KH, int KW>
+__device__ __forceinline__ void pool_cell(const float (&gv)[KH][KW], const float (&pv)[KH][KW], bool wd_on, float wd,
+                                          float &mean, float &sq) {
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < KH; i++) {
+#pragma unroll
+        for (int k = 0; k < KW; k++) {
+            const float x = wd_on ? __fmaf_rn(wd, pv[i][k], gv[i][k]) : gv[i][k];
+            s1 = __fadd_rn(s1, x);
+            s2 = __fadd_rn(s2, __fmul_rn(x, x));
+        }
+    }
+    const float div = (float)(KH * KW);
+    mean = __fdiv_rn(s1, div);
+    sq = __fdiv_rn(s2, div);
+}
+
+template <int KH, int KW>
+__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, float mean, float sq, float *Mrow,
+                                         float *Vrow, int j, bool own) {
+    const smo_hyper &hp = d.hp;
+    float m, v;
+    if (d.kind == SMO_KIND_POOLED8) {
+        const uint32_t b = fast_div(cell, d.div_B);
+        m = dequant1(d.mq_in[cell], dequant_step(d.ms_in[b]));
+        v = dequant1(d.vq_in[cell], dequant_step(d.vs_in[b]));
+    } else {
+        m = d.m_in[cell];
+        v = d.v_in[cell];
+    }
+    m = ema(m, mean, hp.beta1, hp.omb1);
+    v = ema(v, sq, hp.beta2, hp.omb2);
+    Mrow[j] = m;
+    Vrow[j] = v;
+    if (own && d.kind == SMO_KIND_POOLED32) {
+        d.m_out[cell] = m;
+        d.v_out[cell] = v;
+    }
+}
 
 // Phase 1 of compact row c: post-EMA m, v into Mrow/Vrow (shared memory).
 // `own` rows also write the fp32 state (POOLED32); look-ahead rows only read.
-template <int KH, int KW>
-__device__ __forceinline__ void phase1(const FusedDesc &d, int64_t c, float *Mrow, float *Vrow, bool own) {
-    const int64_t w = d.w, W = d.W;
-    const float *gb = d.g + c * KH * W;
-    const float *pb = d.p + c * KH * W;
-    const int64_t cell0 = c * w;
-    const smo_hyper &hp = d.hp;
-    const bool q8 = (d.kind == SMO_KIND_POOLED8);
-    const float div = (float)(KH * KW);
-    for (int64_t j = threadIdx.x; j < w; j += kFusedThreads) {
-        float s1 = 0.0f, s2 = 0.0f;
-        float gv[KH][KW], pv[KH][KW];
+// CELLS cells per thread per iteration keep CELLS*KH*KW*2 loads in flight.
+template <int KH, int KW, int CELLS>
+__device__ __forceinline__ void phase1(const FusedDesc &d, int c, float *Mrow, float *Vrow, bool own) {
+    const int w = d.w;
+    const int64_t W = d.W;
+    const float *gb = d.g + (int64_t)c * KH * W;
+    const float *pb = d.p + (int64_t)c * KH * W;
+    const uint32_t cell0 = (uint32_t)c * (uint32_t)w;
+    const bool wd_on = d.hp.wd_on != 0;
+    const float wd = d.hp.weight_decay;
+    for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * kFusedThreads) {
+        float gv[CELLS][KH][KW], pv[CELLS][KH][KW];
 #pragma unroll
-        for (int i = 0; i < KH; i++) load_row<KW>(gb + i * W + j * KW, gv[i]);
-        if (hp.wd_on) {
+        for (int u = 0; u < CELLS; u++) {
+            const int j = j0 + u * kFusedThreads;
+            if (u == 0 || j < w) {
 #pragma unroll
-            for (int i = 0; i < KH; i++) load_param<KW>(pb + i * W + j * KW, pv[i], false);
-        }
-#pragma unroll
-        for (int i = 0; i < KH; i++) {
-#pragma unroll
-            for (int k = 0; k < KW; k++) {
-                const float x = hp.wd_on ? __fmaf_rn(hp.weight_decay, pv[i][k], gv[i][k]) : gv[i][k];
-                s1 = __fadd_rn(s1, x);
-                s2 = __fadd_rn(s2, __fmul_rn(x, x));
+                for (int i = 0; i < KH; i++) load_grad_row<KW>(gb + i * W + (int64_t)j * KW, gv[u][i]);
             }
         }
-        const float mean = __fdiv_rn(s1, div), sq = __fdiv_rn(s2, div);
-        const int64_t cell = cell0 + j;
-        float m, v;
-        if (q8) {
-            const int64_t b = cell / d.B;
-            m = dequant1(d.mq_in[cell], dequant_step(d.ms_in[b]));
-            v = dequant1(d.vq_in[cell], dequant_step(d.vs_in[b]));
-        } else {
-            m = d.m_in[cell];
-            v = d.v_in[cell];
+        if (wd_on) {
+#pragma unroll
+            for (int u = 0; u < CELLS; u++) {
+                const int j = j0 + u * kFusedThreads;
+                if (u == 0 || j < w) {
+#pragma unroll
+                    for (int i = 0; i < KH; i++) load_param_row<KW, false>(pb + i * W + (int64_t)j * KW, pv[u][i]);
+                }
+            }
         }
-        m = ema(m, mean, hp.beta1, hp.omb1);
-        v = ema(v, sq, hp.beta2, hp.omb2);
-        Mrow[j] = m;
-        Vrow[j] = v;
-        if (own && !q8) {
-            d.m_out[cell] = m;
-            d.v_out[cell] = v;
+#pragma unroll
+        for (int u = 0; u < CELLS; u++) {
+            const int j = j0 + u * kFusedThreads;
+            if (u == 0 || j < w) {
+                float mean, sq;
+                pool_cell<KH, KW>(gv[u], pv[u], wd_on, wd, mean, sq);
+                ema_cell<KH, KW>(d, cell0 + j, mean, sq, Mrow, Vrow, j, own);
+            }
         }
     }
 }
 
 // Requantise the int8 blocks that compact row c completes.  A block spans at
 // most two compact rows (q_block <= w), both still in the ring.
-__device__ __forceinline__ void requant_row(const FusedDesc &d, int64_t c, const float *Mc, const float *Vc,
+__device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const float *Mc, const float *Vc,
                                             const float *Mp, const float *Vp) {
-    const int64_t w = d.w, B = d.B, C = d.h * d.w;
-    int64_t b_lo = (c * w) / B;
-    int64_t b_hi = ((c + 1) * w) / B;
+    const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
+    uint32_t b_lo = fast_div((uint32_t)c * w, d.div_B);
+    uint32_t b_hi = fast_div(((uint32_t)c + 1u) * w, d.div_B);
     if (c == d.h - 1 && C % B != 0) b_hi = C / B + 1;  // the zero-padded last block
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (int64_t b = b_lo + warp; b < b_hi; b += kFusedThreads / 32) {
+    for (uint32_t b = b_lo + warp; b < b_hi; b += kFusedThreads / 32) {
         float am = 0.0f, av = 0.0f;
-        for (int64_t k = lane; k < B; k += 32) {
-            const int64_t cell = b * B + k;
+        for (uint32_t k = lane; k < B; k += 32) {
+            const uint32_t cell = b * B + k;
             if (cell >= C) break;
-            const int64_t row = cell / w, col = cell - row * w;
-            const float m = row == c ? Mc[col] : Mp[col];
-            const float v = row == c ? Vc[col] : Vp[col];
-            am = absmax_acc(am, m);
-            av = absmax_acc(av, v);
+            const uint32_t row = fast_div(cell, d.div_w), col = cell - row * w;
+            const bool cur = (int)row == c;
+            am = absmax_acc(am, cur ? Mc[col] : Mp[col]);
+            av = absmax_acc(av, cur ? Vc[col] : Vp[col]);
         }
         const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
-        for (int64_t k = lane; k < B; k += 32) {
-            const int64_t cell = b * B + k;
+        for (uint32_t k = lane; k < B; k += 32) {
+            const uint32_t cell = b * B + k;
             float m = 0.0f, v = 0.0f;
             if (cell < C) {
-                const int64_t row = cell / w, col = cell - row * w;
-                m = row == c ? Mc[col] : Mp[col];
-                v = row == c ? Vc[col] : Vp[col];
+                const uint32_t row = fast_div(cell, d.div_w), col = cell - row * w;
+                const bool cur = (int)row == c;
+                m = cur ? Mc[col] : Mp[col];
+                v = cur ? Vc[col] : Vp[col];
             }
             d.mq_out[cell] = quantize1(m, sm);
             d.vq_out[cell] = quantize1(v, sv);
@@ -246,15 +304,24 @@ struct RowCo {
     float l0, l1;
 };
 
+// Width-pass weights of output column t of a KW-wide window (power-of-two KW):
+// exactly torch's src = (q + 0.5)/KW - 0.5 split into floor and fraction.
+template <int KW>
+__device__ __forceinline__ float col_l1(int t) {
+    return (t + 0.5f) / KW + (t < KW / 2 ? 0.5f : -0.5f);
+}
+
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
-// c-1 (M[0]), c (M[1]), c+1 (M[2]); absent rows are never addressed.
+// c-1 (M[0]), c (M[1]), c+1 (M[2]) in shared memory; absent rows are never
+// addressed by the row weights.
 template <int KH, int KW>
-__device__ __forceinline__ void phase2(const FusedDesc &d, int64_t c, const float *const M[3], const float *const V[3],
-                                       RowCo *rowco) {
-    const int64_t w = d.w, W = d.W;
+__device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *const M[3], const float *const V[3],
+                                       RowCo *rowco, float rcp_sbc2) {
+    const int w = d.w;
+    const int64_t W = d.W;
     if (threadIdx.x < KH) {
         int small;
-        const Coef rc = row_coef(c * KH + threadIdx.x, d.H, d.h, d.W, d.band, small);
+        const Coef rc = row_coef((int64_t)c * KH + threadIdx.x, d.H, d.h, d.W, d.band, small);
         RowCo r;
         r.s0 = (int)(rc.i0 - (c - 1));
         r.s1 = (int)(rc.i1 - (c - 1));
@@ -264,37 +331,44 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int64_t c, const floa
     }
     __syncthreads();
     const smo_hyper &hp = d.hp;
-    for (int64_t j = threadIdx.x; j < w; j += kFusedThreads) {
-        // width pass for the three compact rows
+    const bool has[3] = {M[0] != nullptr, true, M[2] != nullptr};
+    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+        float *pbase = d.p + (int64_t)c * KH * W + (int64_t)j * KW;
+        float pv[KH][KW];
+#pragma unroll
+        for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
+        // width pass of the three compact rows; left half of the window reads
+        // columns (j-1, j), right half (j, j+1), clamped at the edges as torch does
+        const int jr = j + 1 < w ? j + 1 : w - 1;
+        const int la = j > 0 ? j - 1 : 0;
+        const int lb = j > 0 ? j : jr;
         float hm[3][KW], hv[3][KW];
 #pragma unroll
-        for (int t = 0; t < KW; t++) {
-            const int64_t q = j * KW + t;
-            float real = __fmaf_rn(d.col_scale, __fadd_rn((float)q, 0.5f), -0.5f);
-            real = real < 0.0f ? 0.0f : real;
-            int64_t i0 = (int64_t)floorf(real);
-            i0 = i0 > w - 1 ? w - 1 : i0;
-            float l1 = __fsub_rn(real, (float)i0);
-            l1 = l1 < 0.0f ? 0.0f : (l1 > 1.0f ? 1.0f : l1);
-            const float l0 = __fsub_rn(1.0f, l1);
-            const int64_t i1 = i0 + (i0 < w - 1 ? 1 : 0);
+        for (int s = 0; s < 3; s++) {
+            if (!has[s]) {
 #pragma unroll
-            for (int s = 0; s < 3; s++) {
-                if (M[s]) {
-                    hm[s][t] = __fmaf_rn(M[s][i0], l0, __fmul_rn(M[s][i1], l1));
-                    hv[s][t] = __fmaf_rn(V[s][i0], l0, __fmul_rn(V[s][i1], l1));
+                for (int t = 0; t < KW; t++) hm[s][t] = hv[s][t] = 0.0f;
+                continue;
+            }
+            const float ma = M[s][la], mb = M[s][lb], mc = M[s][j], md = M[s][jr];
+            const float va = V[s][la], vb = V[s][lb], vc = V[s][j], vd = V[s][jr];
+#pragma unroll
+            for (int t = 0; t < KW; t++) {
+                if (t < KW / 2) {
+                    const float l1 = j > 0 ? col_l1<KW>(t) : 0.0f;
+                    const float l0 = j > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
+                    hm[s][t] = __fmaf_rn(ma, l0, __fmul_rn(mb, l1));
+                    hv[s][t] = __fmaf_rn(va, l0, __fmul_rn(vb, l1));
                 } else {
-                    hm[s][t] = 0.0f;
-                    hv[s][t] = 0.0f;
+                    const float l1 = col_l1<KW>(t), l0 = 1.0f - col_l1<KW>(t);
+                    hm[s][t] = __fmaf_rn(mc, l0, __fmul_rn(md, l1));
+                    hv[s][t] = __fmaf_rn(vc, l0, __fmul_rn(vd, l1));
                 }
             }
         }
 #pragma unroll
         for (int i = 0; i < KH; i++) {
             const RowCo rc = rowco[i];
-            float *prow = d.p + (c * KH + i) * W + j * KW;
-            float pv[KW];
-            load_param<KW>(prow, pv, true);
 #pragma unroll
             for (int t = 0; t < KW; t++) {
                 const float a_m = rc.s0 == 0 ? hm[0][t] : hm[1][t];
@@ -303,52 +377,51 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int64_t c, const floa
                 const float b_v = rc.s1 == 1 ? hv[1][t] : hv[2][t];
                 const float mh = __fmaf_rn(a_m, rc.l0, __fmul_rn(b_m, rc.l1));
                 const float vh = __fmaf_rn(a_v, rc.l0, __fmul_rn(b_v, rc.l1));
-                pv[t] = adam_write(pv[t], mh, clamp_min0(vh), hp);
+                pv[i][t] = adam_write_rc(pv[i][t], mh, clamp_min0(vh), hp, rcp_sbc2);
             }
-            store_param<KW>(prow, pv);
+            store_param_row<KW>(pbase + i * W, pv[i]);
         }
     }
     __syncthreads();
 }
 
-template <int KH, int KW>
-__device__ void process_strip(const FusedDesc &d, int64_t sidx, int64_t gstrip, unsigned int epoch, float *smem,
-                              RowCo *rowco, WsHeader *hdr, unsigned int *flags, float *halo, int64_t wait_iters) {
-    const int64_t w = d.w, h = d.h;
-    const int64_t c0 = sidx * d.L;
-    const int64_t c1 = c0 + d.L < h ? c0 + d.L : h;
+template <int KH, int KW, int CELLS>
+__device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float *ring,
+                              float *head, RowCo *rowco, WsHeader *hdr, unsigned int *flags, float *halo,
+                              int64_t wait_iters) {
+    const int w = d.w, h = d.h;
+    const int c0 = sidx * d.L;
+    const int c1 = c0 + d.L < h ? c0 + d.L : h;
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
-    float *ring = smem;          // 3 slots x (m row, v row)
-    float *head = smem + 6 * w;  // rows c0-1, c0, c0+1
-    auto RM = [&](int64_t c) { return ring + 2 * (c % 3) * w; };
-    auto RV = [&](int64_t c) { return ring + (2 * (c % 3) + 1) * w; };
-    float *HM[3] = {head, head + 2 * w, head + 4 * w};
-    float *HV[3] = {head + w, head + 3 * w, head + 5 * w};
-
-    auto copy_row = [&](int64_t c, int slot) {
+    const float rcp_sbc2 = __frcp_rn(d.hp.sqrt_bc2);
+    auto RM = [&](int c) { return ring + 2 * (c % 3) * w; };
+    auto RV = [&](int c) { return ring + (2 * (c % 3) + 1) * w; };
+    // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
+    // strip's first row is written at the end
+    auto save_head = [&](int c, int slot) {
         const float *sm = RM(c), *sv = RV(c);
-        for (int64_t j = threadIdx.x; j < w; j += kFusedThreads) {
-            HM[slot][j] = sm[j];
-            HV[slot][j] = sv[j];
+        float *dst = head + slot * 2 * w;
+        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+            __stcg(dst + j, sm[j]);
+            __stcg(dst + w + j, sv[j]);
         }
     };
 
-    // first row of the strip
-    phase1<KH, KW>(d, c0, RM(c0), RV(c0), true);
+    phase1<KH, KW, CELLS>(d, c0, RM(c0), RV(c0), true);
     __syncthreads();
     if (q8) requant_row(d, c0, RM(c0), RV(c0), nullptr, nullptr);
-    copy_row(c0, 1);
+    save_head(c0, 0);
     __syncthreads();
 
-    for (int64_t c = c0 + 1; c < c1; c++) {
-        phase1<KH, KW>(d, c, RM(c), RV(c), true);
+    for (int c = c0 + 1; c < c1; c++) {
+        phase1<KH, KW, CELLS>(d, c, RM(c), RV(c), true);
         __syncthreads();
         if (q8) requant_row(d, c, RM(c), RV(c), RM(c - 1), RV(c - 1));
-        if (c == c0 + 1) copy_row(c, 2);
+        if (c == c0 + 1) save_head(c, 1);
         if (c - 1 > c0) {
             const float *M[3] = {RM(c - 2), RM(c - 1), RM(c)};
             const float *V[3] = {RV(c - 2), RV(c - 1), RV(c)};
-            phase2<KH, KW>(d, c - 1, M, V, rowco);  // ends with __syncthreads
+            phase2<KH, KW>(d, c - 1, M, V, rowco, rcp_sbc2);  // ends with __syncthreads
         } else {
             __syncthreads();
         }
@@ -356,15 +429,15 @@ __device__ void process_strip(const FusedDesc &d, int64_t sidx, int64_t gstrip, 
 
     if (c1 < h) {
         // look-ahead: the next strip's first row, from its g, p and old state
-        phase1<KH, KW>(d, c1, RM(c1), RV(c1), false);
+        phase1<KH, KW, CELLS>(d, c1, RM(c1), RV(c1), false);
         __syncthreads();
-        if (c1 == c0 + 1) copy_row(c1, 2);
+        if (c1 == c0 + 1) save_head(c1, 1);
         // publish this strip's last row for the next strip (after the look-ahead read)
-        float *out = halo + d.halo_off + sidx * 2 * w;
+        float *out = halo + d.halo_off + (int64_t)sidx * 2 * w;
         const float *sm = RM(c1 - 1), *sv = RV(c1 - 1);
-        for (int64_t j = threadIdx.x; j < w; j += kFusedThreads) {
-            out[j] = sm[j];
-            out[w + j] = sv[j];
+        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+            __stcg(out + j, sm[j]);
+            __stcg(out + w + j, sv[j]);
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -374,31 +447,42 @@ __device__ void process_strip(const FusedDesc &d, int64_t sidx, int64_t gstrip, 
     }
 
     if (c1 - 1 > c0) {
-        const float *M[3] = {c1 - 2 >= 0 ? RM(c1 - 2) : nullptr, RM(c1 - 1), c1 < h ? RM(c1) : nullptr};
-        const float *V[3] = {c1 - 2 >= 0 ? RV(c1 - 2) : nullptr, RV(c1 - 1), c1 < h ? RV(c1) : nullptr};
-        phase2<KH, KW>(d, c1 - 1, M, V, rowco);
+        const float *M[3] = {RM(c1 - 2), RM(c1 - 1), c1 < h ? RM(c1) : nullptr};
+        const float *V[3] = {RV(c1 - 2), RV(c1 - 1), c1 < h ? RV(c1) : nullptr};
+        phase2<KH, KW>(d, c1 - 1, M, V, rowco, rcp_sbc2);
     }
 
-    // deferred first row: needs the previous strip's last row
+    // deferred first row: rows c0-1 (the previous strip's published row), c0 and
+    // c0+1 go back into ring slots 0, 1, 2
+    __shared__ int s_ok;
     if (c0 > 0) {
-        __shared__ int s_ok;
         if (threadIdx.x == 0) {
             const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
             if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
             s_ok = ok;
         }
         __syncthreads();
-        const float *in = halo + d.halo_off + (sidx - 1) * 2 * w;
-        for (int64_t j = threadIdx.x; j < w; j += kFusedThreads) {
-            HM[0][j] = s_ok ? __ldcg(in + j) : 0.0f;
-            HV[0][j] = s_ok ? __ldcg(in + w + j) : 0.0f;
-        }
-        __syncthreads();
     }
     {
-        const float *M[3] = {c0 > 0 ? HM[0] : nullptr, HM[1], c0 + 1 < h ? HM[2] : nullptr};
-        const float *V[3] = {c0 > 0 ? HV[0] : nullptr, HV[1], c0 + 1 < h ? HV[2] : nullptr};
-        phase2<KH, KW>(d, c0, M, V, rowco);
+        const float *prev = halo + d.halo_off + (int64_t)(sidx - 1) * 2 * w;
+        const bool ok = c0 > 0 && s_ok;
+        const bool next = c0 + 1 < h;
+        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+            if (c0 > 0) {
+                ring[j] = ok ? __ldcg(prev + j) : 0.0f;
+                ring[w + j] = ok ? __ldcg(prev + w + j) : 0.0f;
+            }
+            ring[2 * w + j] = __ldcg(head + j);
+            ring[3 * w + j] = __ldcg(head + w + j);
+            if (next) {
+                ring[4 * w + j] = __ldcg(head + 2 * w + j);
+                ring[5 * w + j] = __ldcg(head + 3 * w + j);
+            }
+        }
+        __syncthreads();
+        const float *M[3] = {c0 > 0 ? ring : nullptr, ring + 2 * w, next ? ring + 4 * w : nullptr};
+        const float *V[3] = {c0 > 0 ? ring + w : nullptr, ring + 3 * w, next ? ring + 5 * w : nullptr};
+        phase2<KH, KW>(d, c0, M, V, rowco, rcp_sbc2);
     }
 }
 
@@ -411,15 +495,16 @@ __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s)
     return lo;
 }
 
-template <int KH, int KW>
-__global__ void __launch_bounds__(kFusedThreads) fused_step_kernel(const __grid_constant__ FusedBatch b,
-                                                                    WsHeader *hdr, unsigned int *flags, float *halo,
-                                                                    int64_t wait_iters) {
-    extern __shared__ float smem[];
+template <int KH, int KW, int CELLS, int MINB>
+__global__ void __launch_bounds__(kFusedThreads, MINB)
+    fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
+                      float *heads, int64_t head_stride, int64_t wait_iters) {
+    extern __shared__ float ring[];
     __shared__ RowCo rowco[KH];
     __shared__ int64_t s_strip;
     __shared__ unsigned int s_epoch;
     if (threadIdx.x == 0) s_epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
+    float *head = heads + (int64_t)blockIdx.x * head_stride;
     const int64_t total = b.strip_start[b.n];
     for (;;) {
         if (threadIdx.x == 0) s_strip = (int64_t)atomicAdd(&hdr->next_item, 1u);
@@ -429,7 +514,8 @@ __global__ void __launch_bounds__(kFusedThreads) fused_step_kernel(const __grid_
         __syncthreads();
         if (s >= total) break;
         const int t = find_strip_tensor(b, s);
-        process_strip<KH, KW>(b.d[t], s - b.strip_start[t], s, epoch, smem, rowco, hdr, flags, halo, wait_iters);
+        process_strip<KH, KW, CELLS>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags, halo,
+                              wait_iters);
     }
     if (threadIdx.x == 0) {
         __threadfence();
@@ -457,6 +543,16 @@ static int64_t gcd64(int64_t a, int64_t b) {
     return a;
 }
 
+static FastDiv make_fast_div(uint32_t d) {
+    FastDiv f;
+    f.d = d;
+    uint32_t l = 0;
+    while (l < 32 && (1ull << l) < d) l++;
+    f.l = l;
+    f.m = (uint32_t)(((((uint64_t)1 << l) - d) << 32) / d + 1);
+    return f;
+}
+
 static int64_t strip_rows(const smo_tensor &t) {
     int64_t align = 1;
     if (t.kind == SMO_KIND_POOLED8) align = t.q_block / gcd64(t.comp_cols, t.q_block);
@@ -473,6 +569,7 @@ bool fused_takes(const smo_tensor &t) {
     if (!supported_window(kh) || !supported_window(kw)) return false;
     if (t.cols <= 128) return false;  // torch's small-output interpolation order
     if (t.comp_cols > kMaxFusedCols) return false;
+    if (t.comp_rows * t.comp_cols >= ((int64_t)1 << 31)) return false;  // 32-bit cell indices
     if (t.kind == SMO_KIND_POOLED8 && t.q_block > t.comp_cols) return false;
     const size_t a = kw % 4 == 0 ? 16 : 8;
     if ((uintptr_t)t.param % a || (uintptr_t)t.grad % a) return false;
@@ -498,57 +595,79 @@ static int window_key(const smo_tensor &t) {
     return (int)((t.rows / t.comp_rows) * 16 + (t.cols / t.comp_cols));
 }
 
+// Tuning override for measurements: SMO_B200_FUSED_VARIANT=1 selects two
+// cells per iteration at 2 CTAs/SM (128 registers) for every window.
+static int fused_variant() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("SMO_B200_FUSED_VARIANT");
+        v = e ? atoi(e) : 0;
+    }
+    return v;
+}
+
+static int device_sm_count() {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 148;
+    return sms;
+}
+
+static inline size_t align_up(size_t x) { return (x + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
+
+// Workspace after the header: [flags: one word per strip][published rows:
+// 2*w floats per strip][head rows: 4*max_w floats per CTA].  Sized for the
+// whole set; each window-group launch reuses the space.
 size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
-    // flags (one word per strip) and published rows (2*w floats per strip),
-    // sized for the whole set (each window-group launch reuses the space).
     size_t strips = 0, halo_floats = 0;
+    int64_t max_w = 0;
     for (int32_t i = 0; i < n; i++) {
         if (!fused_takes(t[i])) continue;
         const int64_t s = num_strips(t[i]);
         strips += (size_t)s;
         halo_floats += (size_t)s * 2 * (size_t)t[i].comp_cols;
+        max_w = max_w > t[i].comp_cols ? max_w : t[i].comp_cols;
     }
     if (!strips) return 0;
-    const size_t flags_bytes = (strips * sizeof(unsigned int) + kScratchAlign - 1) / kScratchAlign * kScratchAlign;
-    return flags_bytes + halo_floats * sizeof(float);
+    const size_t ctas = (size_t)device_sm_count() * kMaxFusedCtasPerSm;
+    return align_up(strips * sizeof(unsigned int)) + align_up(halo_floats * sizeof(float)) +
+           ctas * 4 * (size_t)max_w * sizeof(float);
 }
 
 template <int KH, int KW>
-static int launch_fused_group(FusedBatch &b, int64_t max_w, char *ws, cudaStream_t stream) {
-    // ring (3 rows) + head (3 rows), each row an m and a v vector of w floats
-    const size_t smem = (size_t)12 * max_w * sizeof(float);
-    auto kern = fused_step_kernel<KH, KW>;
+static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
+    const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
+    // 16-element windows: one cell per thread-iteration at 3 CTAs/SM (80
+    // registers); smaller windows: two cells per iteration
+    auto kern = (KH * KW >= 16) ? fused_step_kernel<KH, KW, 1, 3> : fused_step_kernel<KH, KW, 2, 3>;
+    if (fused_variant() == 1) kern = fused_step_kernel<KH, KW, 2, 2>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     int per_sm = 0;
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedThreads, smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (per_sm < 1) per_sm = 1;
+    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
     const int64_t strips = b.strip_start[b.n];
-    int64_t grid = (int64_t)sms * per_sm;
+    int64_t grid = (int64_t)device_sm_count() * per_sm;
     grid = grid < strips ? grid : strips;
     WsHeader *hdr = (WsHeader *)ws;
-    size_t flags_bytes = 0;
-    {
-        // flags sit right after the header; published rows after the flags
-        flags_bytes = ((size_t)strips * sizeof(unsigned int) + kScratchAlign - 1) / kScratchAlign * kScratchAlign;
-    }
-    unsigned int *flags = (unsigned int *)(ws + kWsHeader);
-    float *halo = (float *)(ws + kWsHeader + flags_bytes);
-    kern<<<(unsigned)grid, kFusedThreads, smem, stream>>>(b, hdr, flags, halo, kDefaultWaitIters);
+    char *body = ws + kWsHeader;
+    unsigned int *flags = (unsigned int *)body;
+    body += align_up((size_t)strips * sizeof(unsigned int));
+    float *halo = (float *)body;
+    body += align_up(halo_floats * sizeof(float));
+    float *heads = (float *)body;
+    kern<<<(unsigned)grid, kFusedThreads, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;
     return SMO_OK;
 }
 
-static int dispatch(int key, FusedBatch &b, int64_t max_w, char *ws, cudaStream_t stream) {
+static int dispatch(int key, FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
     switch (key) {
 #define SMO_FUSED_CASE(KH, KW) \
-    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, ws, stream);
+    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, halo_floats, ws, stream);
         SMO_FUSED_CASE(2, 2) SMO_FUSED_CASE(2, 4) SMO_FUSED_CASE(2, 8)
         SMO_FUSED_CASE(4, 2) SMO_FUSED_CASE(4, 4) SMO_FUSED_CASE(4, 8)
         SMO_FUSED_CASE(8, 2) SMO_FUSED_CASE(8, 4) SMO_FUSED_CASE(8, 8)
@@ -564,12 +683,13 @@ static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off) {
     f.mq_in = t.m_q_in; f.ms_in = t.m_s_in; f.vq_in = t.v_q_in; f.vs_in = t.v_s_in;
     f.mq_out = t.m_q_out; f.ms_out = t.m_s_out; f.vq_out = t.v_q_out; f.vs_out = t.v_s_out;
     f.m_in = t.m_in; f.v_in = t.v_in; f.m_out = t.m_out; f.v_out = t.v_out;
-    f.H = t.rows; f.W = t.cols; f.h = t.comp_rows; f.w = t.comp_cols;
-    f.B = t.q_block;
-    f.band = t.interp_band;
-    f.L = strip_rows(t);
+    f.H = t.rows; f.W = t.cols; f.band = t.interp_band;
+    f.h = (int32_t)t.comp_rows; f.w = (int32_t)t.comp_cols;
+    f.B = t.kind == SMO_KIND_POOLED8 ? (int32_t)t.q_block : 1;
+    f.L = (int32_t)strip_rows(t);
+    f.div_B = make_fast_div((uint32_t)f.B);
+    f.div_w = make_fast_div((uint32_t)f.w);
     f.halo_off = halo_off;
-    f.col_scale = (float)t.comp_cols / (float)t.cols;
     f.kind = t.kind;
     f.hp = t.hp;
 }
@@ -599,7 +719,7 @@ int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaSt
         }
         // tensors of the same window left over (batch full) start a new batch when
         // the scan reaches them
-        const int st = dispatch(key, batch, max_w, ws, stream);
+        const int st = dispatch(key, batch, max_w, (size_t)halo_off, ws, stream);
         if (st != SMO_OK) return st;
     }
     return SMO_OK;
