@@ -156,21 +156,57 @@ __device__ __forceinline__ void report_error(WsHeader *hdr, unsigned int code, u
     if (atomicCAS(&hdr->error, 0u, code) == 0u) hdr->error_where = where;
 }
 
-// x / c for a per-tensor constant c with r = RN(1/c): Markstein's correction
-// (q0 = RN(x r), rem = x - q0 c exactly by fma, q = RN(q0 + rem r)) returns
-// the correctly rounded quotient for finite x away from under/overflow; here
-// x = sqrt(v) >= 0 and c = sqrt(1 - beta2^t) in (0, 1], so only x = +inf
-// needs the general division.
-__device__ __forceinline__ float div_by_const(float x, float c, float r) {
-    if (x == __int_as_float(0x7f800000)) return __fdiv_rn(x, c);
+// x / c with r = RN(1/c): Markstein's correction (q0 = RN(x r), rem = x - q0 c
+// exactly by fma, q = RN(q0 + rem r)) returns the correctly rounded quotient
+// whenever x and the quotient are normal numbers (Markstein 1990; Muller et
+// al., Handbook of Floating-Point Arithmetic, the correction step of
+// reciprocal-based division).  Callers keep to that range or only use results
+// for which a last-bit difference cannot matter; x = +-inf passes through.
+__device__ __forceinline__ float div_rcp(float x, float c, float r) {
     const float q0 = __fmul_rn(x, r);
     const float rem = __fmaf_rn(-q0, c, x);
-    return __fmaf_rn(rem, r, q0);
+    const float q = __fmaf_rn(rem, r, q0);
+    return fabsf(x) == __int_as_float(0x7f800000) ? __fdiv_rn(x, c) : q;
 }
 
+// sqrt(v) / sqrt(1 - beta2^t): v >= 0, c in (0, 1], so sqrt(v) is 0, normal,
+// +inf or NaN and the quotient stays normal.
 __device__ __forceinline__ float adam_write_rc(float p, float m, float v, const smo_hyper &hp, float rcp_sbc2) {
-    const float d = __fadd_rn(div_by_const(__fsqrt_rn(v), hp.sqrt_bc2, rcp_sbc2), hp.eps);
+    const float d = __fadd_rn(div_rcp(__fsqrt_rn(v), hp.sqrt_bc2, rcp_sbc2), hp.eps);
     return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
+}
+
+// q * (s / 127) with s >= 1e-12 (a clamped block scale), so s / 127 is normal
+constexpr float kRcp127 = 0x1.020408p-7f;  // RN(1/127)
+__device__ __forceinline__ float dequant_rc(int8_t q, float s) {
+    return __fmul_rn((float)q, div_rcp(s, 127.0f, kRcp127));
+}
+
+// round(x / s * 127) with the dead-zone lift and clamp (spatial_8bit.py:97-106),
+// given rs = RN(1/s).  A quotient too small for Markstein's bound is far below
+// the first rounding threshold 0.5/127, so the code is the same either way;
+// a non-finite scale takes the IEEE division.
+__device__ __forceinline__ int8_t quantize_rc(float x, float s, float rs, bool s_finite) {
+    const float q = s_finite ? div_rcp(x, s, rs) : __fdiv_rn(x, s);
+    float r = rintf(__fmul_rn(q, 127.0f));
+    if (r == 0.0f && x != 0.0f && x == x) r = x > 0.0f ? 1.0f : -1.0f;
+    r = r > 127.0f ? 127.0f : r;
+    r = r < -127.0f ? -127.0f : r;
+    return (r == r) ? (int8_t)(int)r : (int8_t)0;
+}
+
+// Hint the next compact row's gradient and parameter rows into L2 (TMA bulk
+// prefetch; no shared memory, no completion to wait for).
+template <int KH>
+__device__ __forceinline__ void prefetch_row_l2(const FusedDesc &d, int c) {
+    const int i = threadIdx.x;
+    if (i < 2 * KH) {
+        const float *base = (i < KH ? d.g : d.p) + ((int64_t)c * KH + (i % KH)) * d.W;
+        if (i >= KH && !d.hp.wd_on) return;
+        const uint32_t bytes = (uint32_t)((d.W * 4) & ~(int64_t)15);
+        if (((uintptr_t)base & 15) == 0 && bytes > 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(bytes) : "memory");
+    }
 }
 
 // ---------------------------------------------------------------- phases
@@ -188,9 +224,11 @@ __device__ __forceinline__ void pool_cell(const float (&gv)[KH][KW], const float
             s2 = __fadd_rn(s2, __fmul_rn(x, x));
         }
     }
-    const float div = (float)(KH * KW);
-    mean = __fdiv_rn(s1, div);
-    sq = __fdiv_rn(s2, div);
+    // KH*KW is a power of two: multiplying by its exact reciprocal rounds to the
+    // same value as avg_pool2d's division
+    constexpr float inv = 1.0f / (KH * KW);
+    mean = __fmul_rn(s1, inv);
+    sq = __fmul_rn(s2, inv);
 }
 
 template <int KH, int KW>
@@ -200,8 +238,8 @@ __device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, floa
     float m, v;
     if (d.kind == SMO_KIND_POOLED8) {
         const uint32_t b = fast_div(cell, d.div_B);
-        m = dequant1(d.mq_in[cell], dequant_step(d.ms_in[b]));
-        v = dequant1(d.vq_in[cell], dequant_step(d.vs_in[b]));
+        m = dequant_rc(d.mq_in[cell], d.ms_in[b]);
+        v = dequant_rc(d.vq_in[cell], d.vs_in[b]);
     } else {
         m = d.m_in[cell];
         v = d.v_in[cell];
@@ -262,47 +300,82 @@ __device__ __forceinline__ void phase1(const FusedDesc &d, int c, float *Mrow, f
 
 // Requantise the int8 blocks that compact row c completes.  A block spans at
 // most two compact rows (q_block <= w), both still in the ring.
+__device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, int c, const float *Mc, const float *Vc,
+                                              const float *Mp, const float *Vp, bool aligned) {
+    const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rowbase = (uint32_t)c * w;
+    float am = 0.0f, av = 0.0f;
+    for (uint32_t k = lane; k < B; k += 32) {
+        const uint32_t cell = b * B + k;
+        if (cell >= C) break;
+        float m, v;
+        if (aligned) {
+            m = Mc[cell - rowbase];
+            v = Vc[cell - rowbase];
+        } else {
+            const bool cur = cell >= rowbase;
+            m = cur ? Mc[cell - rowbase] : Mp[cell + w - rowbase];
+            v = cur ? Vc[cell - rowbase] : Vp[cell + w - rowbase];
+        }
+        am = absmax_acc(am, m);
+        av = absmax_acc(av, v);
+    }
+    const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
+    const bool fm = sm < __int_as_float(0x7f800000), fv = sv < __int_as_float(0x7f800000);
+    const float rm = __frcp_rn(sm), rv = __frcp_rn(sv);
+    for (uint32_t k = lane; k < B; k += 32) {
+        const uint32_t cell = b * B + k;
+        float m = 0.0f, v = 0.0f;
+        if (cell < C) {
+            if (aligned) {
+                m = Mc[cell - rowbase];
+                v = Vc[cell - rowbase];
+            } else {
+                const bool cur = cell >= rowbase;
+                m = cur ? Mc[cell - rowbase] : Mp[cell + w - rowbase];
+                v = cur ? Vc[cell - rowbase] : Vp[cell + w - rowbase];
+            }
+        }
+        d.mq_out[cell] = quantize_rc(m, sm, rm, fm);
+        d.vq_out[cell] = quantize_rc(v, sv, rv, fv);
+    }
+    if (lane == 0) {
+        d.ms_out[b] = sm;
+        d.vs_out[b] = sv;
+    }
+}
+
 __device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const float *Mc, const float *Vc,
                                             const float *Mp, const float *Vp) {
     const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
-    uint32_t b_lo = fast_div((uint32_t)c * w, d.div_B);
+    const uint32_t b_lo = fast_div((uint32_t)c * w, d.div_B);
     uint32_t b_hi = fast_div(((uint32_t)c + 1u) * w, d.div_B);
     if (c == d.h - 1 && C % B != 0) b_hi = C / B + 1;  // the zero-padded last block
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (uint32_t b = b_lo + warp; b < b_hi; b += kFusedThreads / 32) {
-        float am = 0.0f, av = 0.0f;
-        for (uint32_t k = lane; k < B; k += 32) {
-            const uint32_t cell = b * B + k;
-            if (cell >= C) break;
-            const uint32_t row = fast_div(cell, d.div_w), col = cell - row * w;
-            const bool cur = (int)row == c;
-            am = absmax_acc(am, cur ? Mc[col] : Mp[col]);
-            av = absmax_acc(av, cur ? Vc[col] : Vp[col]);
-        }
-        const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
-        for (uint32_t k = lane; k < B; k += 32) {
-            const uint32_t cell = b * B + k;
-            float m = 0.0f, v = 0.0f;
-            if (cell < C) {
-                const uint32_t row = fast_div(cell, d.div_w), col = cell - row * w;
-                const bool cur = (int)row == c;
-                m = cur ? Mc[col] : Mp[col];
-                v = cur ? Vc[col] : Vp[col];
-            }
-            d.mq_out[cell] = quantize1(m, sm);
-            d.vq_out[cell] = quantize1(v, sv);
-        }
-        if (lane == 0) {
-            d.ms_out[b] = sm;
-            d.vs_out[b] = sv;
-        }
-    }
+    const bool aligned = (w % B) == 0;                  // blocks never leave the row
+    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += kFusedThreads / 32)
+        requant_block(d, b, c, Mc, Vc, Mp, Vp, aligned);
 }
 
 struct RowCo {
     int s0, s1;  // ring-relative rows (0: c-1, 1: c, 2: c+1)
     float l0, l1;
 };
+
+// Row weights of the KH output rows of compact row c (threads 0..KH-1).
+template <int KH>
+__device__ __forceinline__ void compute_rowco(const FusedDesc &d, int c, RowCo *dst) {
+    if (threadIdx.x < KH) {
+        int small;
+        const Coef rc = row_coef((int64_t)c * KH + threadIdx.x, d.H, d.h, d.W, d.band, small);
+        RowCo r;
+        r.s0 = (int)(rc.i0 - (c - 1));
+        r.s1 = (int)(rc.i1 - (c - 1));
+        r.l0 = rc.l0;
+        r.l1 = rc.l1;
+        dst[threadIdx.x] = r;
+    }
+}
 
 // Width-pass weights of output column t of a KW-wide window (power-of-two KW):
 // exactly torch's src = (q + 0.5)/KW - 0.5 split into floor and fraction.
@@ -312,44 +385,28 @@ __device__ __forceinline__ float col_l1(int t) {
 }
 
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
-// c-1 (M[0]), c (M[1]), c+1 (M[2]) in shared memory; absent rows are never
-// addressed by the row weights.
+// c-1 (M[0]), c (M[1]), c+1 (M[2]) in shared memory (an absent neighbour row
+// is passed as row c and never weighted).  Row weights come from `rowco`.
 template <int KH, int KW>
 __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *const M[3], const float *const V[3],
-                                       RowCo *rowco, float rcp_sbc2) {
+                                       const RowCo *rowco, float rcp_sbc2) {
     const int w = d.w;
     const int64_t W = d.W;
-    if (threadIdx.x < KH) {
-        int small;
-        const Coef rc = row_coef((int64_t)c * KH + threadIdx.x, d.H, d.h, d.W, d.band, small);
-        RowCo r;
-        r.s0 = (int)(rc.i0 - (c - 1));
-        r.s1 = (int)(rc.i1 - (c - 1));
-        r.l0 = rc.l0;
-        r.l1 = rc.l1;
-        rowco[threadIdx.x] = r;
-    }
-    __syncthreads();
     const smo_hyper &hp = d.hp;
-    const bool has[3] = {M[0] != nullptr, true, M[2] != nullptr};
     for (int j = threadIdx.x; j < w; j += kFusedThreads) {
         float *pbase = d.p + (int64_t)c * KH * W + (int64_t)j * KW;
         float pv[KH][KW];
 #pragma unroll
         for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
-        // width pass of the three compact rows; left half of the window reads
-        // columns (j-1, j), right half (j, j+1), clamped at the edges as torch does
+        // width pass of the three compact rows; the left half of the window
+        // reads columns (j-1, j), the right half (j, j+1), clamped at the edges
+        // exactly as torch's index/lambda computation does
         const int jr = j + 1 < w ? j + 1 : w - 1;
         const int la = j > 0 ? j - 1 : 0;
         const int lb = j > 0 ? j : jr;
         float hm[3][KW], hv[3][KW];
 #pragma unroll
         for (int s = 0; s < 3; s++) {
-            if (!has[s]) {
-#pragma unroll
-                for (int t = 0; t < KW; t++) hm[s][t] = hv[s][t] = 0.0f;
-                continue;
-            }
             const float ma = M[s][la], mb = M[s][lb], mc = M[s][j], md = M[s][jr];
             const float va = V[s][la], vb = V[s][lb], vc = V[s][j], vd = V[s][jr];
 #pragma unroll
@@ -369,12 +426,13 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *c
 #pragma unroll
         for (int i = 0; i < KH; i++) {
             const RowCo rc = rowco[i];
+            const bool lo0 = rc.s0 == 0, lo1 = rc.s1 == 1;  // uniform across the CTA
 #pragma unroll
             for (int t = 0; t < KW; t++) {
-                const float a_m = rc.s0 == 0 ? hm[0][t] : hm[1][t];
-                const float b_m = rc.s1 == 1 ? hm[1][t] : hm[2][t];
-                const float a_v = rc.s0 == 0 ? hv[0][t] : hv[1][t];
-                const float b_v = rc.s1 == 1 ? hv[1][t] : hv[2][t];
+                const float a_m = lo0 ? hm[0][t] : hm[1][t];
+                const float b_m = lo1 ? hm[1][t] : hm[2][t];
+                const float a_v = lo0 ? hv[0][t] : hv[1][t];
+                const float b_v = lo1 ? hv[1][t] : hv[2][t];
                 const float mh = __fmaf_rn(a_m, rc.l0, __fmul_rn(b_m, rc.l1));
                 const float vh = __fmaf_rn(a_v, rc.l0, __fmul_rn(b_v, rc.l1));
                 pv[i][t] = adam_write_rc(pv[i][t], mh, clamp_min0(vh), hp, rcp_sbc2);
@@ -382,16 +440,18 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *c
             store_param_row<KW>(pbase + i * W, pv[i]);
         }
     }
-    __syncthreads();
 }
 
+// One strip: phase-1 rows r = c0 .. c1 (c1 = look-ahead row, when it exists),
+// each followed by phase 2 of row r-1; then the strip's first row.
 template <int KH, int KW, int CELLS>
 __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float *ring,
-                              float *head, RowCo *rowco, WsHeader *hdr, unsigned int *flags, float *halo,
+                              float *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
                               int64_t wait_iters) {
     const int w = d.w, h = d.h;
     const int c0 = sidx * d.L;
     const int c1 = c0 + d.L < h ? c0 + d.L : h;
+    const int last = c1 < h ? c1 : c1 - 1;  // last phase-1 row
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
     const float rcp_sbc2 = __frcp_rn(d.hp.sqrt_bc2);
     auto RM = [&](int c) { return ring + 2 * (c % 3) * w; };
@@ -407,83 +467,80 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         }
     };
 
-    phase1<KH, KW, CELLS>(d, c0, RM(c0), RV(c0), true);
-    __syncthreads();
-    if (q8) requant_row(d, c0, RM(c0), RV(c0), nullptr, nullptr);
-    save_head(c0, 0);
-    __syncthreads();
-
-    for (int c = c0 + 1; c < c1; c++) {
-        phase1<KH, KW, CELLS>(d, c, RM(c), RV(c), true);
+    for (int r = c0; r <= last; r++) {
+        const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
+        if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
+        if (r < last) prefetch_row_l2<KH>(d, r + 1);
+        phase1<KH, KW, CELLS>(d, r, RM(r), RV(r), r < c1);
         __syncthreads();
-        if (q8) requant_row(d, c, RM(c), RV(c), RM(c - 1), RV(c - 1));
-        if (c == c0 + 1) save_head(c, 1);
-        if (c - 1 > c0) {
-            const float *M[3] = {RM(c - 2), RM(c - 1), RM(c)};
-            const float *V[3] = {RV(c - 2), RV(c - 1), RV(c)};
-            phase2<KH, KW>(d, c - 1, M, V, rowco, rcp_sbc2);  // ends with __syncthreads
+        if (r < c1) {
+            if (q8) requant_row(d, r, RM(r), RV(r), r > c0 ? RM(r - 1) : nullptr, r > c0 ? RV(r - 1) : nullptr);
+            if (r == c0) save_head(r, 0);
+            if (r == c0 + 1) save_head(r, 1);
         } else {
+            // look-ahead row: keep it as the strip's second row if the strip has
+            // one row, then publish this strip's last row for the next strip
+            // (after the look-ahead read of that strip's parameters and state)
+            if (r == c0 + 1) save_head(r, 1);
+            float *out = halo + d.halo_off + (int64_t)sidx * 2 * w;
+            const float *sm = RM(c1 - 1), *sv = RV(c1 - 1);
+            for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+                __stcg(out + j, sm[j]);
+                __stcg(out + w + j, sv[j]);
+            }
             __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                store_release(flags + gstrip, epoch);
+            }
         }
-    }
-
-    if (c1 < h) {
-        // look-ahead: the next strip's first row, from its g, p and old state
-        phase1<KH, KW, CELLS>(d, c1, RM(c1), RV(c1), false);
-        __syncthreads();
-        if (c1 == c0 + 1) save_head(c1, 1);
-        // publish this strip's last row for the next strip (after the look-ahead read)
-        float *out = halo + d.halo_off + (int64_t)sidx * 2 * w;
-        const float *sm = RM(c1 - 1), *sv = RV(c1 - 1);
-        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
-            __stcg(out + j, sm[j]);
-            __stcg(out + w + j, sv[j]);
+        if (do2) {
+            const float *M[3] = {RM(r - 2), RM(r - 1), RM(r)};
+            const float *V[3] = {RV(r - 2), RV(r - 1), RV(r)};
+            phase2<KH, KW>(d, r - 1, M, V, rowco[(r - 1) & 1], rcp_sbc2);
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            __threadfence();
-            store_release(flags + gstrip, epoch);
-        }
+    }
+    if (c1 == h && c1 - 1 > c0) {
+        // the tensor's last row: no look-ahead row below it
+        compute_rowco<KH>(d, c1 - 1, rowco[(c1 - 1) & 1]);
+        __syncthreads();
+        const float *M[3] = {RM(c1 - 2), RM(c1 - 1), RM(c1 - 1)};
+        const float *V[3] = {RV(c1 - 2), RV(c1 - 1), RV(c1 - 1)};
+        phase2<KH, KW>(d, c1 - 1, M, V, rowco[(c1 - 1) & 1], rcp_sbc2);
+        __syncthreads();
     }
 
-    if (c1 - 1 > c0) {
-        const float *M[3] = {RM(c1 - 2), RM(c1 - 1), c1 < h ? RM(c1) : nullptr};
-        const float *V[3] = {RV(c1 - 2), RV(c1 - 1), c1 < h ? RV(c1) : nullptr};
-        phase2<KH, KW>(d, c1 - 1, M, V, rowco, rcp_sbc2);
-    }
-
-    // deferred first row: rows c0-1 (the previous strip's published row), c0 and
-    // c0+1 go back into ring slots 0, 1, 2
+    // deferred first row: rows c0-1 (the previous strip's published row), c0
+    // and c0+1 go back into ring slots 0, 1, 2
     __shared__ int s_ok;
-    if (c0 > 0) {
-        if (threadIdx.x == 0) {
-            const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
-            if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
-            s_ok = ok;
-        }
-        __syncthreads();
+    compute_rowco<KH>(d, c0, rowco[c0 & 1]);
+    if (c0 > 0 && threadIdx.x == 0) {
+        const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
+        if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
+        s_ok = ok;
     }
-    {
-        const float *prev = halo + d.halo_off + (int64_t)(sidx - 1) * 2 * w;
-        const bool ok = c0 > 0 && s_ok;
-        const bool next = c0 + 1 < h;
-        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
-            if (c0 > 0) {
-                ring[j] = ok ? __ldcg(prev + j) : 0.0f;
-                ring[w + j] = ok ? __ldcg(prev + w + j) : 0.0f;
-            }
-            ring[2 * w + j] = __ldcg(head + j);
-            ring[3 * w + j] = __ldcg(head + w + j);
-            if (next) {
-                ring[4 * w + j] = __ldcg(head + 2 * w + j);
-                ring[5 * w + j] = __ldcg(head + 3 * w + j);
-            }
+    __syncthreads();
+    const float *prev = halo + d.halo_off + (int64_t)(sidx > 0 ? sidx - 1 : 0) * 2 * w;
+    const bool ok = c0 > 0 && s_ok;
+    const bool next = c0 + 1 < h;
+    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+        if (c0 > 0) {
+            ring[j] = ok ? __ldcg(prev + j) : 0.0f;
+            ring[w + j] = ok ? __ldcg(prev + w + j) : 0.0f;
         }
-        __syncthreads();
-        const float *M[3] = {c0 > 0 ? ring : nullptr, ring + 2 * w, next ? ring + 4 * w : nullptr};
-        const float *V[3] = {c0 > 0 ? ring + w : nullptr, ring + 3 * w, next ? ring + 5 * w : nullptr};
-        phase2<KH, KW>(d, c0, M, V, rowco, rcp_sbc2);
+        ring[2 * w + j] = __ldcg(head + j);
+        ring[3 * w + j] = __ldcg(head + w + j);
+        if (next) {
+            ring[4 * w + j] = __ldcg(head + 2 * w + j);
+            ring[5 * w + j] = __ldcg(head + 3 * w + j);
+        }
     }
+    __syncthreads();
+    const float *M[3] = {c0 > 0 ? ring : ring + 2 * w, ring + 2 * w, next ? ring + 4 * w : ring + 2 * w};
+    const float *V[3] = {c0 > 0 ? ring + w : ring + 3 * w, ring + 3 * w, next ? ring + 5 * w : ring + 3 * w};
+    phase2<KH, KW>(d, c0, M, V, rowco[c0 & 1], rcp_sbc2);
+    __syncthreads();
 }
 
 __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s) {
@@ -500,7 +557,7 @@ __global__ void __launch_bounds__(kFusedThreads, MINB)
     fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
                       float *heads, int64_t head_stride, int64_t wait_iters) {
     extern __shared__ float ring[];
-    __shared__ RowCo rowco[KH];
+    __shared__ RowCo rowco[2][KH];
     __shared__ int64_t s_strip;
     __shared__ unsigned int s_epoch;
     if (threadIdx.x == 0) s_epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
