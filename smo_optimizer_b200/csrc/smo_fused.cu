@@ -156,17 +156,19 @@ __device__ __forceinline__ void report_error(WsHeader *hdr, unsigned int code, u
     if (atomicCAS(&hdr->error, 0u, code) == 0u) hdr->error_where = where;
 }
 
-// x / c with r = RN(1/c): Markstein's correction (q0 = RN(x r), rem = x - q0 c
-// exactly by fma, q = RN(q0 + rem r)) returns the correctly rounded quotient
-// whenever x and the quotient are normal numbers (Markstein 1990; Muller et
-// al., Handbook of Floating-Point Arithmetic, the correction step of
-// reciprocal-based division).  Callers keep to that range or only use results
-// for which a last-bit difference cannot matter; x = +-inf passes through.
+// x / c with r = RN(1/c) for a finite c > 0: Markstein's correction
+// (q0 = RN(x r), rem = x - q0 c exactly by fma, q = RN(q0 + rem r)) returns the
+// correctly rounded quotient whenever x and the quotient are normal numbers
+// (Markstein 1990; Muller et al., Handbook of Floating-Point Arithmetic, the
+// correction step of reciprocal-based division).  Callers keep to that range
+// or only use results for which a last-bit difference cannot matter.  x = +-inf
+// gives +-inf (x / c for finite c > 0) and NaN stays NaN; no IEEE division is
+// evaluated on any path.
 __device__ __forceinline__ float div_rcp(float x, float c, float r) {
     const float q0 = __fmul_rn(x, r);
     const float rem = __fmaf_rn(-q0, c, x);
     const float q = __fmaf_rn(rem, r, q0);
-    return fabsf(x) == __int_as_float(0x7f800000) ? __fdiv_rn(x, c) : q;
+    return fabsf(x) == __int_as_float(0x7f800000) ? x : q;
 }
 
 // sqrt(v) / sqrt(1 - beta2^t): v >= 0, c in (0, 1], so sqrt(v) is 0, normal,
@@ -184,10 +186,14 @@ __device__ __forceinline__ float dequant_rc(int8_t q, float s) {
 
 // round(x / s * 127) with the dead-zone lift and clamp (spatial_8bit.py:97-106),
 // given rs = RN(1/s).  A quotient too small for Markstein's bound is far below
-// the first rounding threshold 0.5/127, so the code is the same either way;
-// a non-finite scale takes the IEEE division.
-__device__ __forceinline__ int8_t quantize_rc(float x, float s, float rs, bool s_finite) {
-    const float q = s_finite ? div_rcp(x, s, rs) : __fdiv_rn(x, s);
+// the first rounding threshold 0.5/127, so the code is the same either way.  A
+// non-finite block scale comes from non-finite moments: x / inf is a signed
+// zero for finite x and NaN for x = +-inf; x / NaN is NaN (stored as code 0).
+__device__ __forceinline__ int8_t quantize_rc(float x, float s, float rs) {
+    const float inf = __int_as_float(0x7f800000);
+    float q = div_rcp(x, s, rs);
+    if (s == inf) q = fabsf(x) == inf ? __int_as_float(0x7fffffff) : copysignf(0.0f, x);
+    if (s != s) q = s;
     float r = rintf(__fmul_rn(q, 127.0f));
     if (r == 0.0f && x != 0.0f && x == x) r = x > 0.0f ? 1.0f : -1.0f;
     r = r > 127.0f ? 127.0f : r;
@@ -322,7 +328,6 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
         av = absmax_acc(av, v);
     }
     const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
-    const bool fm = sm < __int_as_float(0x7f800000), fv = sv < __int_as_float(0x7f800000);
     const float rm = __frcp_rn(sm), rv = __frcp_rn(sv);
     for (uint32_t k = lane; k < B; k += 32) {
         const uint32_t cell = b * B + k;
@@ -337,8 +342,8 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
                 v = cur ? Vc[cell - rowbase] : Vp[cell + w - rowbase];
             }
         }
-        d.mq_out[cell] = quantize_rc(m, sm, rm, fm);
-        d.vq_out[cell] = quantize_rc(v, sv, rv, fv);
+        d.mq_out[cell] = quantize_rc(m, sm, rm);
+        d.vq_out[cell] = quantize_rc(v, sv, rv);
     }
     if (lane == 0) {
         d.ms_out[b] = sm;
