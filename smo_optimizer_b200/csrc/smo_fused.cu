@@ -156,6 +156,16 @@ __device__ __forceinline__ void report_error(WsHeader *hdr, unsigned int code, u
     if (atomicCAS(&hdr->error, 0u, code) == 0u) hdr->error_where = where;
 }
 
+// ---------------------------------------------------------------- packed arithmetic
+//
+// The m and v channels see the same weights everywhere (EMA, width pass,
+// height pass), so each (m, v) pair travels as one float2 and is computed with
+// Blackwell's packed fp32x2 instructions; every lane is an ordinary correctly
+// rounded fp32 operation, so results are bit-identical to the scalar sequence.
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 splat(float a) { return make_float2(a, a); }
+
 // x / c with r = RN(1/c) for a finite c > 0: Markstein's correction
 // (q0 = RN(x r), rem = x - q0 c exactly by fma, q = RN(q0 + rem r)) returns the
 // correctly rounded quotient whenever x and the quotient are normal numbers
@@ -166,22 +176,40 @@ __device__ __forceinline__ void report_error(WsHeader *hdr, unsigned int code, u
 // evaluated on any path.
 __device__ __forceinline__ float div_rcp(float x, float c, float r) {
     const float q0 = __fmul_rn(x, r);
-    const float rem = __fmaf_rn(-q0, c, x);
+    const float rem = __fmaf_rn(q0, -c, x);
     const float q = __fmaf_rn(rem, r, q0);
     return fabsf(x) == __int_as_float(0x7f800000) ? x : q;
 }
 
-// sqrt(v) / sqrt(1 - beta2^t): v >= 0, c in (0, 1], so sqrt(v) is 0, normal,
-// +inf or NaN and the quotient stays normal.
-__device__ __forceinline__ float adam_write_rc(float p, float m, float v, const smo_hyper &hp, float rcp_sbc2) {
-    const float d = __fadd_rn(div_rcp(__fsqrt_rn(v), hp.sqrt_bc2, rcp_sbc2), hp.eps);
-    return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
+// the same for a pair, with per-lane constants (c.x, c.y) and reciprocals
+__device__ __forceinline__ float2 div_rcp2(float2 x, float2 c, float2 r) {
+    const float2 q0 = __fmul2_rn(x, r);
+    const float2 rem = __ffma2_rn(q0, f2(-c.x, -c.y), x);
+    const float2 q = __ffma2_rn(rem, r, q0);
+    const float inf = __int_as_float(0x7f800000);
+    return f2(fabsf(x.x) == inf ? x.x : q.x, fabsf(x.y) == inf ? x.y : q.y);
 }
 
-// q * (s / 127) with s >= 1e-12 (a clamped block scale), so s / 127 is normal
+// The Adam write of two neighbouring elements (spatial_8bit.py:293-297):
+// p + ((-lr/bc1) * m) / (sqrt(v)/sqrt(bc2) + eps).  sqrt(v) is 0, normal, +inf
+// or NaN and sqrt(bc2) is in (0, 1], so the divide-by-constant stays normal.
+struct AdamK {
+    float2 sbc2, rcp_sbc2, eps, ns;
+};
+
+__device__ __forceinline__ float2 adam_write2(float2 p, float2 m, float2 v, const AdamK &k) {
+    const float2 sv = f2(__fsqrt_rn(v.x), __fsqrt_rn(v.y));
+    const float2 d = __fadd2_rn(div_rcp2(sv, k.sbc2, k.rcp_sbc2), k.eps);
+    const float2 a = __fmul2_rn(k.ns, m);
+    return __fadd2_rn(p, f2(__fdiv_rn(a.x, d.x), __fdiv_rn(a.y, d.y)));
+}
+
+// codes * (scales / 127) for an (m, v) pair; scales >= 1e-12 (clamped block
+// scales), so scale / 127 is normal
 constexpr float kRcp127 = 0x1.020408p-7f;  // RN(1/127)
-__device__ __forceinline__ float dequant_rc(int8_t q, float s) {
-    return __fmul_rn((float)q, div_rcp(s, 127.0f, kRcp127));
+__device__ __forceinline__ float2 dequant2(int8_t qm, int8_t qv, float sm, float sv) {
+    const float2 t = div_rcp2(f2(sm, sv), splat(127.0f), splat(kRcp127));
+    return __fmul2_rn(f2((float)qm, (float)qv), t);
 }
 
 // round(x / s * 127) with the dead-zone lift and clamp (spatial_8bit.py:97-106),
@@ -217,60 +245,52 @@ __device__ __forceinline__ void prefetch_row_l2(const FusedDesc &d, int c) {
 
 // ---------------------------------------------------------------- phases
 
-template <int KH, int KW>
-__device__ __forceinline__ void pool_cell(const float (&gv)[KH][KW], const float (&pv)[KH][KW], bool wd_on, float wd,
-                                          float &mean, float &sq) {
-    float s1 = 0.0f, s2 = 0.0f;
+// (sum x, sum x*x) of one KH x KW window in row-major order from +0, times
+// 1/(KH*KW) (a power of two: the same value as avg_pool2d's division)
+template <int KH, int KW, bool WD>
+__device__ __forceinline__ float2 pool_cell(const float (&gv)[KH][KW], const float (&pv)[KH][KW], float wd) {
+    float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < KH; i++) {
 #pragma unroll
         for (int k = 0; k < KW; k++) {
-            const float x = wd_on ? __fmaf_rn(wd, pv[i][k], gv[i][k]) : gv[i][k];
-            s1 = __fadd_rn(s1, x);
-            s2 = __fadd_rn(s2, __fmul_rn(x, x));
+            const float x = WD ? __fmaf_rn(wd, pv[i][k], gv[i][k]) : gv[i][k];
+            acc = __fadd2_rn(acc, f2(x, __fmul_rn(x, x)));
         }
     }
-    // KH*KW is a power of two: multiplying by its exact reciprocal rounds to the
-    // same value as avg_pool2d's division
     constexpr float inv = 1.0f / (KH * KW);
-    mean = __fmul_rn(s1, inv);
-    sq = __fmul_rn(s2, inv);
+    return __fmul2_rn(acc, splat(inv));
 }
 
-template <int KH, int KW>
-__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, float mean, float sq, float *Mrow,
-                                         float *Vrow, int j, bool own) {
+// dequant of the old moments, EMA, post-EMA pair into the ring row
+__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, float2 pooled, float2 *row, int j,
+                                         bool own) {
     const smo_hyper &hp = d.hp;
-    float m, v;
+    float2 mv;
     if (d.kind == SMO_KIND_POOLED8) {
         const uint32_t b = fast_div(cell, d.div_B);
-        m = dequant_rc(d.mq_in[cell], d.ms_in[b]);
-        v = dequant_rc(d.vq_in[cell], d.vs_in[b]);
+        mv = dequant2(d.mq_in[cell], d.vq_in[cell], d.ms_in[b], d.vs_in[b]);
     } else {
-        m = d.m_in[cell];
-        v = d.v_in[cell];
+        mv = f2(d.m_in[cell], d.v_in[cell]);
     }
-    m = ema(m, mean, hp.beta1, hp.omb1);
-    v = ema(v, sq, hp.beta2, hp.omb2);
-    Mrow[j] = m;
-    Vrow[j] = v;
+    mv = __ffma2_rn(f2(hp.omb1, hp.omb2), pooled, __fmul2_rn(mv, f2(hp.beta1, hp.beta2)));
+    row[j] = mv;
     if (own && d.kind == SMO_KIND_POOLED32) {
-        d.m_out[cell] = m;
-        d.v_out[cell] = v;
+        d.m_out[cell] = mv.x;
+        d.v_out[cell] = mv.y;
     }
 }
 
-// Phase 1 of compact row c: post-EMA m, v into Mrow/Vrow (shared memory).
+// Phase 1 of compact row c: post-EMA (m, v) into `row` (shared memory).
 // `own` rows also write the fp32 state (POOLED32); look-ahead rows only read.
 // CELLS cells per thread per iteration keep CELLS*KH*KW*2 loads in flight.
-template <int KH, int KW, int CELLS>
-__device__ __forceinline__ void phase1(const FusedDesc &d, int c, float *Mrow, float *Vrow, bool own) {
+template <int KH, int KW, int CELLS, bool WD>
+__device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row, bool own) {
     const int w = d.w;
     const int64_t W = d.W;
     const float *gb = d.g + (int64_t)c * KH * W;
     const float *pb = d.p + (int64_t)c * KH * W;
     const uint32_t cell0 = (uint32_t)c * (uint32_t)w;
-    const bool wd_on = d.hp.wd_on != 0;
     const float wd = d.hp.weight_decay;
     for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * kFusedThreads) {
         float gv[CELLS][KH][KW], pv[CELLS][KH][KW];
@@ -280,13 +300,7 @@ __device__ __forceinline__ void phase1(const FusedDesc &d, int c, float *Mrow, f
             if (u == 0 || j < w) {
 #pragma unroll
                 for (int i = 0; i < KH; i++) load_grad_row<KW>(gb + i * W + (int64_t)j * KW, gv[u][i]);
-            }
-        }
-        if (wd_on) {
-#pragma unroll
-            for (int u = 0; u < CELLS; u++) {
-                const int j = j0 + u * kFusedThreads;
-                if (u == 0 || j < w) {
+                if (WD) {
 #pragma unroll
                     for (int i = 0; i < KH; i++) load_param_row<KW, false>(pb + i * W + (int64_t)j * KW, pv[u][i]);
                 }
@@ -295,19 +309,21 @@ __device__ __forceinline__ void phase1(const FusedDesc &d, int c, float *Mrow, f
 #pragma unroll
         for (int u = 0; u < CELLS; u++) {
             const int j = j0 + u * kFusedThreads;
-            if (u == 0 || j < w) {
-                float mean, sq;
-                pool_cell<KH, KW>(gv[u], pv[u], wd_on, wd, mean, sq);
-                ema_cell<KH, KW>(d, cell0 + j, mean, sq, Mrow, Vrow, j, own);
-            }
+            if (u == 0 || j < w) ema_cell(d, cell0 + j, pool_cell<KH, KW, WD>(gv[u], pv[u], wd), row, j, own);
         }
     }
 }
 
+template <int KH, int KW, int CELLS>
+__device__ __forceinline__ void phase1(const FusedDesc &d, int c, float2 *row, bool own) {
+    if (d.hp.wd_on) phase1_wd<KH, KW, CELLS, true>(d, c, row, own);
+    else phase1_wd<KH, KW, CELLS, false>(d, c, row, own);
+}
+
 // Requantise the int8 blocks that compact row c completes.  A block spans at
 // most two compact rows (q_block <= w), both still in the ring.
-__device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, int c, const float *Mc, const float *Vc,
-                                              const float *Mp, const float *Vp, bool aligned) {
+__device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, int c, const float2 *Rc,
+                                              const float2 *Rp, bool aligned) {
     const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
     const int lane = threadIdx.x & 31;
     const uint32_t rowbase = (uint32_t)c * w;
@@ -315,35 +331,18 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
     for (uint32_t k = lane; k < B; k += 32) {
         const uint32_t cell = b * B + k;
         if (cell >= C) break;
-        float m, v;
-        if (aligned) {
-            m = Mc[cell - rowbase];
-            v = Vc[cell - rowbase];
-        } else {
-            const bool cur = cell >= rowbase;
-            m = cur ? Mc[cell - rowbase] : Mp[cell + w - rowbase];
-            v = cur ? Vc[cell - rowbase] : Vp[cell + w - rowbase];
-        }
-        am = absmax_acc(am, m);
-        av = absmax_acc(av, v);
+        const float2 mv = (aligned || cell >= rowbase) ? Rc[cell - rowbase] : Rp[cell + w - rowbase];
+        am = absmax_acc(am, mv.x);
+        av = absmax_acc(av, mv.y);
     }
     const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
     const float rm = __frcp_rn(sm), rv = __frcp_rn(sv);
     for (uint32_t k = lane; k < B; k += 32) {
         const uint32_t cell = b * B + k;
-        float m = 0.0f, v = 0.0f;
-        if (cell < C) {
-            if (aligned) {
-                m = Mc[cell - rowbase];
-                v = Vc[cell - rowbase];
-            } else {
-                const bool cur = cell >= rowbase;
-                m = cur ? Mc[cell - rowbase] : Mp[cell + w - rowbase];
-                v = cur ? Vc[cell - rowbase] : Vp[cell + w - rowbase];
-            }
-        }
-        d.mq_out[cell] = quantize_rc(m, sm, rm);
-        d.vq_out[cell] = quantize_rc(v, sv, rv);
+        float2 mv = f2(0.0f, 0.0f);
+        if (cell < C) mv = (aligned || cell >= rowbase) ? Rc[cell - rowbase] : Rp[cell + w - rowbase];
+        d.mq_out[cell] = quantize_rc(mv.x, sm, rm);
+        d.vq_out[cell] = quantize_rc(mv.y, sv, rv);
     }
     if (lane == 0) {
         d.ms_out[b] = sm;
@@ -351,15 +350,14 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
     }
 }
 
-__device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const float *Mc, const float *Vc,
-                                            const float *Mp, const float *Vp) {
+__device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const float2 *Rc, const float2 *Rp) {
     const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
     const uint32_t b_lo = fast_div((uint32_t)c * w, d.div_B);
     uint32_t b_hi = fast_div(((uint32_t)c + 1u) * w, d.div_B);
     if (c == d.h - 1 && C % B != 0) b_hi = C / B + 1;  // the zero-padded last block
     const bool aligned = (w % B) == 0;                  // blocks never leave the row
     for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += kFusedThreads / 32)
-        requant_block(d, b, c, Mc, Vc, Mp, Vp, aligned);
+        requant_block(d, b, c, Rc, Rp, aligned);
 }
 
 struct RowCo {
@@ -390,41 +388,36 @@ __device__ __forceinline__ float col_l1(int t) {
 }
 
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
-// c-1 (M[0]), c (M[1]), c+1 (M[2]) in shared memory (an absent neighbour row
+// c-1 (R[0]), c (R[1]), c+1 (R[2]) in shared memory (an absent neighbour row
 // is passed as row c and never weighted).  Row weights come from `rowco`.
 template <int KH, int KW>
-__device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *const M[3], const float *const V[3],
-                                       const RowCo *rowco, float rcp_sbc2) {
+__device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
+                                       const AdamK &ak) {
     const int w = d.w;
     const int64_t W = d.W;
-    const smo_hyper &hp = d.hp;
     for (int j = threadIdx.x; j < w; j += kFusedThreads) {
         float *pbase = d.p + (int64_t)c * KH * W + (int64_t)j * KW;
         float pv[KH][KW];
 #pragma unroll
         for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
-        // width pass of the three compact rows; the left half of the window
-        // reads columns (j-1, j), the right half (j, j+1), clamped at the edges
-        // exactly as torch's index/lambda computation does
+        // width pass of the three compact rows: the left half of the window
+        // interpolates columns (j-1, j), the right half (j, j+1), clamped at the
+        // edges exactly as torch's index/lambda computation does
         const int jr = j + 1 < w ? j + 1 : w - 1;
         const int la = j > 0 ? j - 1 : 0;
-        const int lb = j > 0 ? j : jr;
-        float hm[3][KW], hv[3][KW];
+        float2 h[3][KW];
 #pragma unroll
         for (int s = 0; s < 3; s++) {
-            const float ma = M[s][la], mb = M[s][lb], mc = M[s][j], md = M[s][jr];
-            const float va = V[s][la], vb = V[s][lb], vc = V[s][j], vd = V[s][jr];
+            const float2 left = R[s][la], mid = R[s][j], right = R[s][jr];
+            const float2 x = j > 0 ? mid : right;
 #pragma unroll
             for (int t = 0; t < KW; t++) {
                 if (t < KW / 2) {
                     const float l1 = j > 0 ? col_l1<KW>(t) : 0.0f;
                     const float l0 = j > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
-                    hm[s][t] = __fmaf_rn(ma, l0, __fmul_rn(mb, l1));
-                    hv[s][t] = __fmaf_rn(va, l0, __fmul_rn(vb, l1));
+                    h[s][t] = __ffma2_rn(left, splat(l0), __fmul2_rn(x, splat(l1)));
                 } else {
-                    const float l1 = col_l1<KW>(t), l0 = 1.0f - col_l1<KW>(t);
-                    hm[s][t] = __fmaf_rn(mc, l0, __fmul_rn(md, l1));
-                    hv[s][t] = __fmaf_rn(vc, l0, __fmul_rn(vd, l1));
+                    h[s][t] = __ffma2_rn(mid, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(right, splat(col_l1<KW>(t))));
                 }
             }
         }
@@ -432,15 +425,19 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *c
         for (int i = 0; i < KH; i++) {
             const RowCo rc = rowco[i];
             const bool lo0 = rc.s0 == 0, lo1 = rc.s1 == 1;  // uniform across the CTA
+            float2 mh[KW];
 #pragma unroll
             for (int t = 0; t < KW; t++) {
-                const float a_m = lo0 ? hm[0][t] : hm[1][t];
-                const float b_m = lo1 ? hm[1][t] : hm[2][t];
-                const float a_v = lo0 ? hv[0][t] : hv[1][t];
-                const float b_v = lo1 ? hv[1][t] : hv[2][t];
-                const float mh = __fmaf_rn(a_m, rc.l0, __fmul_rn(b_m, rc.l1));
-                const float vh = __fmaf_rn(a_v, rc.l0, __fmul_rn(b_v, rc.l1));
-                pv[i][t] = adam_write_rc(pv[i][t], mh, clamp_min0(vh), hp, rcp_sbc2);
+                const float2 a = lo0 ? h[0][t] : h[1][t];
+                const float2 b = lo1 ? h[1][t] : h[2][t];
+                mh[t] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
+            }
+#pragma unroll
+            for (int t = 0; t < KW; t += 2) {
+                const float2 pn = adam_write2(f2(pv[i][t], pv[i][t + 1]), f2(mh[t].x, mh[t + 1].x),
+                                              f2(clamp_min0(mh[t].y), clamp_min0(mh[t + 1].y)), ak);
+                pv[i][t] = pn.x;
+                pv[i][t + 1] = pn.y;
             }
             store_param_row<KW>(pbase + i * W, pv[i]);
         }
@@ -450,36 +447,37 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float *c
 // One strip: phase-1 rows r = c0 .. c1 (c1 = look-ahead row, when it exists),
 // each followed by phase 2 of row r-1; then the strip's first row.
 template <int KH, int KW, int CELLS>
-__device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float *ring,
-                              float *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
+__device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float2 *ring,
+                              float2 *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
                               int64_t wait_iters) {
     const int w = d.w, h = d.h;
     const int c0 = sidx * d.L;
     const int c1 = c0 + d.L < h ? c0 + d.L : h;
     const int last = c1 < h ? c1 : c1 - 1;  // last phase-1 row
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
-    const float rcp_sbc2 = __frcp_rn(d.hp.sqrt_bc2);
-    auto RM = [&](int c) { return ring + 2 * (c % 3) * w; };
-    auto RV = [&](int c) { return ring + (2 * (c % 3) + 1) * w; };
+    AdamK ak;
+    ak.sbc2 = splat(d.hp.sqrt_bc2);
+    ak.rcp_sbc2 = splat(__frcp_rn(d.hp.sqrt_bc2));
+    ak.eps = splat(d.hp.eps);
+    ak.ns = splat(d.hp.neg_step);
+    auto RR = [&](int c) { return ring + (c % 3) * w; };
+    float2 *pub = reinterpret_cast<float2 *>(halo + d.halo_off) + (int64_t)sidx * w;
     // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
     // strip's first row is written at the end
     auto save_head = [&](int c, int slot) {
-        const float *sm = RM(c), *sv = RV(c);
-        float *dst = head + slot * 2 * w;
-        for (int j = threadIdx.x; j < w; j += kFusedThreads) {
-            __stcg(dst + j, sm[j]);
-            __stcg(dst + w + j, sv[j]);
-        }
+        const float2 *src = RR(c);
+        float2 *dst = head + slot * w;
+        for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(dst + j, src[j]);
     };
 
     for (int r = c0; r <= last; r++) {
         const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
         if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
         if (r < last) prefetch_row_l2<KH>(d, r + 1);
-        phase1<KH, KW, CELLS>(d, r, RM(r), RV(r), r < c1);
+        phase1<KH, KW, CELLS>(d, r, RR(r), r < c1);
         __syncthreads();
         if (r < c1) {
-            if (q8) requant_row(d, r, RM(r), RV(r), r > c0 ? RM(r - 1) : nullptr, r > c0 ? RV(r - 1) : nullptr);
+            if (q8) requant_row(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
             if (r == c0) save_head(r, 0);
             if (r == c0 + 1) save_head(r, 1);
         } else {
@@ -487,12 +485,8 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
             // one row, then publish this strip's last row for the next strip
             // (after the look-ahead read of that strip's parameters and state)
             if (r == c0 + 1) save_head(r, 1);
-            float *out = halo + d.halo_off + (int64_t)sidx * 2 * w;
-            const float *sm = RM(c1 - 1), *sv = RV(c1 - 1);
-            for (int j = threadIdx.x; j < w; j += kFusedThreads) {
-                __stcg(out + j, sm[j]);
-                __stcg(out + w + j, sv[j]);
-            }
+            const float2 *src = RR(c1 - 1);
+            for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(pub + j, src[j]);
             __syncthreads();
             if (threadIdx.x == 0) {
                 __threadfence();
@@ -500,9 +494,8 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
             }
         }
         if (do2) {
-            const float *M[3] = {RM(r - 2), RM(r - 1), RM(r)};
-            const float *V[3] = {RV(r - 2), RV(r - 1), RV(r)};
-            phase2<KH, KW>(d, r - 1, M, V, rowco[(r - 1) & 1], rcp_sbc2);
+            const float2 *R[3] = {RR(r - 2), RR(r - 1), RR(r)};
+            phase2<KH, KW>(d, r - 1, R, rowco[(r - 1) & 1], ak);
         }
         __syncthreads();
     }
@@ -510,9 +503,8 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         // the tensor's last row: no look-ahead row below it
         compute_rowco<KH>(d, c1 - 1, rowco[(c1 - 1) & 1]);
         __syncthreads();
-        const float *M[3] = {RM(c1 - 2), RM(c1 - 1), RM(c1 - 1)};
-        const float *V[3] = {RV(c1 - 2), RV(c1 - 1), RV(c1 - 1)};
-        phase2<KH, KW>(d, c1 - 1, M, V, rowco[(c1 - 1) & 1], rcp_sbc2);
+        const float2 *R[3] = {RR(c1 - 2), RR(c1 - 1), RR(c1 - 1)};
+        phase2<KH, KW>(d, c1 - 1, R, rowco[(c1 - 1) & 1], ak);
         __syncthreads();
     }
 
@@ -526,25 +518,17 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         s_ok = ok;
     }
     __syncthreads();
-    const float *prev = halo + d.halo_off + (int64_t)(sidx > 0 ? sidx - 1 : 0) * 2 * w;
+    const float2 *prev = pub - (sidx > 0 ? w : 0);
     const bool ok = c0 > 0 && s_ok;
     const bool next = c0 + 1 < h;
     for (int j = threadIdx.x; j < w; j += kFusedThreads) {
-        if (c0 > 0) {
-            ring[j] = ok ? __ldcg(prev + j) : 0.0f;
-            ring[w + j] = ok ? __ldcg(prev + w + j) : 0.0f;
-        }
-        ring[2 * w + j] = __ldcg(head + j);
-        ring[3 * w + j] = __ldcg(head + w + j);
-        if (next) {
-            ring[4 * w + j] = __ldcg(head + 2 * w + j);
-            ring[5 * w + j] = __ldcg(head + 3 * w + j);
-        }
+        if (c0 > 0) ring[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
+        ring[w + j] = __ldcg(head + j);
+        if (next) ring[2 * w + j] = __ldcg(head + w + j);
     }
     __syncthreads();
-    const float *M[3] = {c0 > 0 ? ring : ring + 2 * w, ring + 2 * w, next ? ring + 4 * w : ring + 2 * w};
-    const float *V[3] = {c0 > 0 ? ring + w : ring + 3 * w, ring + 3 * w, next ? ring + 5 * w : ring + 3 * w};
-    phase2<KH, KW>(d, c0, M, V, rowco[c0 & 1], rcp_sbc2);
+    const float2 *R[3] = {c0 > 0 ? ring : ring + w, ring + w, next ? ring + 2 * w : ring + w};
+    phase2<KH, KW>(d, c0, R, rowco[c0 & 1], ak);
     __syncthreads();
 }
 
@@ -561,12 +545,12 @@ template <int KH, int KW, int CELLS, int MINB>
 __global__ void __launch_bounds__(kFusedThreads, MINB)
     fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
                       float *heads, int64_t head_stride, int64_t wait_iters) {
-    extern __shared__ float ring[];
+    extern __shared__ float2 ring[];
     __shared__ RowCo rowco[2][KH];
     __shared__ int64_t s_strip;
     __shared__ unsigned int s_epoch;
     if (threadIdx.x == 0) s_epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
-    float *head = heads + (int64_t)blockIdx.x * head_stride;
+    float2 *head = reinterpret_cast<float2 *>(heads + (int64_t)blockIdx.x * head_stride);
     const int64_t total = b.strip_start[b.n];
     for (;;) {
         if (threadIdx.x == 0) s_strip = (int64_t)atomicAdd(&hdr->next_item, 1u);
