@@ -1,0 +1,118 @@
+"""ZeRO-1 host logic on CPU ranks (gloo, world_size 2): the partition, the
+owner-to-all parameter broadcast, and a rank failing before the broadcast.
+
+The CUDA step cannot run on the CPU, so the ranks use a stand-in optimizer
+(plain SGD on their owned tensors); what is under test is the sharding and the
+collective plumbing around the step."""
+
+import os
+import socket
+import time
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from smo_optimizer_b200 import zero
+
+
+class StandIn(torch.optim.Optimizer):
+    def __init__(self, params, lr=0.1, **_):
+        super().__init__(params, dict(lr=lr))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for g in self.param_groups:
+            for p in g["params"]:
+                p.add_(p.grad, alpha=-g["lr"])
+
+
+SHAPES = [(64, 256), (128, 128), (32, 32), (300,), (256, 64), (96, 96), (1024,)]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _params(seed):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(s, generator=g) for s in SHAPES]
+
+
+def _worker(rank, world, port, mode, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    try:
+        params = [torch.nn.Parameter(t) for t in _params(0)]
+        grads = _params(1)
+        for p, g in zip(params, grads):
+            p.grad = g.clone()
+        z = zero.Zero1(params, StandIn, lr=0.5)
+        if mode == "fail" and rank == 1:
+            raise SystemExit(3)  # this rank dies before the broadcast
+        t0 = time.time()
+        try:
+            z.step()
+            out[rank] = ("ok", [p.detach().clone() for p in params], z.owner)
+        except Exception as e:  # the peer is gone: the collective must fail, not hang
+            out[rank] = ("error", type(e).__name__, time.time() - t0)
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def _run(mode):
+    ctx = mp.get_context("spawn")
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+            pytest.fail("a rank hung")
+    return dict(out), [p.exitcode for p in procs]
+
+
+def test_lpt_partition_is_deterministic_and_balanced():
+    costs = [zero.step_bytes(s, "SMO8bit") for s in SHAPES * 5]
+    owner = zero.lpt_partition(costs, 4)
+    assert owner == zero.lpt_partition(costs, 4)
+    loads = zero.rank_loads(costs, owner, 4)
+    assert max(loads) <= min(loads) + max(costs)
+    assert zero.lpt_partition(costs, 1) == [0] * len(costs)
+
+
+def test_step_bytes_formula():
+    # pooled int8, 1024x1024 at k=0.25: 12 B/param + 4 B/cell + 16 B/block
+    assert zero.step_bytes((1024, 1024), "SMO8bit") == 12 * 1024 * 1024 + 4 * 65536 + 16 * 1024
+    assert zero.step_bytes((300,), "SMO8bit") == 28 * 300
+    assert zero.step_bytes((1024, 1024), "SMO", k_ratio=0.5) == 12 * 1024 * 1024 + 16 * 512 * 512
+
+
+def test_zero1_broadcast_makes_replicas_identical():
+    out, codes = _run("ok")
+    assert codes == [0, 0]
+    (s0, p0, own0), (s1, p1, own1) = out[0], out[1]
+    assert s0 == s1 == "ok" and own0 == own1 and set(own0) == {0, 1}
+    expected = [p - 0.5 * g for p, g in zip(_params(0), _params(1))]
+    for a, b, e in zip(p0, p1, expected):
+        assert torch.equal(a, b)
+        assert torch.allclose(a, e)
+
+
+def test_rank_failure_before_broadcast_surfaces_as_error():
+    out, codes = _run("fail")
+    assert codes[1] == 3
+    status = out[0]
+    assert status[0] == "error", status
+    assert status[2] < 60.0
