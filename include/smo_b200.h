@@ -119,6 +119,26 @@ SMO_API int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size
  * stream).  SMO_OK or SMO_ERR_TIMEOUT. */
 SMO_API int smo_workspace_status(void *workspace, void *stream);
 
+/* Bytes of the fixed scratch array behind smo_step_no_alloc(). */
+#define SMO_NO_ALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+
+/* The same step as smo_step() for callers that cannot allocate device memory
+ * (for instance a plug-in that only receives the device pointers of its inputs
+ * and outputs from a host runtime that owns all device memory).  No
+ * counterpart in the reference.
+ * Scratch comes from a 32 MiB array in the library's own device memory, held
+ * on every GPU where the library's device code is loaded until the process
+ * exits; the call allocates nothing.  A step whose smo_workspace_size() exceeds
+ * SMO_NO_ALLOC_SCRATCH_BYTES is rejected with SMO_ERR_WORKSPACE before any work
+ * is enqueued.  The first call on a device resolves that device's copy of the
+ * array (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  All calls share the one array and it keeps the
+ * previous call's contents: calls that overlap on the GPU (other streams,
+ * other threads) race and must be serialised by the caller.  If
+ * device_status is not NULL (a device int32), the step's device-side status
+ * (SMO_OK or SMO_ERR_TIMEOUT) is copied there, in stream order. */
+SMO_API int smo_step_no_alloc(const smo_tensor *tensors, int32_t n, int32_t *device_status, void *stream);
+
 /* ---- stage entry points (same arithmetic as the fused step) ------------ */
 
 /* SMO8bit._quantize_blockwise (spatial_8bit.py:85-107): x[n] -> codes

@@ -80,6 +80,7 @@ def load():
         "smo_abi_version": (ctypes.c_int, []),
         "smo_tensor_struct_size": (sz, []),
         "smo_launch_count": (ctypes.c_uint64, []),
+        "smo_step_no_alloc": (ctypes.c_int, [P, i32, P, P]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)
