@@ -467,11 +467,12 @@ __device__ __forceinline__ void load_p2(const FusedDesc &d, int c, int k, P2Regs
 }
 
 // Phase 2 of (row c, chunk k): the thread's RPT output rows of cell k*CW + j,
-// from the post-EMA rows c-1 (R[0]), c (R[1]), c+1 (R[2]) (an absent neighbour
-// row is passed as row c and never weighted); row weights from `rowco`.
+// from the post-EMA rows c-1 (R0), c (R1), c+1 (R2) (an absent neighbour row is
+// passed as row c and never weighted); row weights from `rowco`.
 template <int KH, int KW>
-__device__ __forceinline__ void phase2(const FusedDesc &d, int c, int k, const float2 *const R[3],
-                                       const RowCo *rowco, const AdamK &ak, const P2Regs<KH, KW> &pr) {
+__device__ __forceinline__ void phase2(const FusedDesc &d, int c, int k, const float2 *R0, const float2 *R1,
+                                       const float2 *R2, const RowCo *rowco, const AdamK &ak,
+                                       const P2Regs<KH, KW> &pr) {
     using G = Geo<KH, KW>;
     constexpr int NR = G::NR;
     const int j = threadIdx.x % G::CW;
@@ -495,7 +496,8 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, int k, const f
     float2 hw[NR][KW];
 #pragma unroll
     for (int q = 0; q < NR; q++) {
-        const float2 *row = R[sa + q];
+        const int sr = sa + q;
+        const float2 *row = sr == 0 ? R0 : (sr == 1 ? R1 : R2);
         const float2 L = row[la], M = row[col], Rr = row[jr];
         const float2 X = col > 0 ? M : Rr;
 #pragma unroll
@@ -546,68 +548,65 @@ struct SharedCtl {
     int ok;
 };
 
-struct StripCtx {
-    const FusedDesc *d;
-    int c0, c1, nk;
-    int nmain, nsteps;  // main steps: rows c0..c1, chunks 0..nk; then nk deferred steps
+// Step cursor of a strip: main steps walk rows c0..c1 (c1 = the look-ahead
+// row, or one past the tensor's last row), chunks 0..nk each; then nk deferred
+// steps rewrite the strip's first row.  Step (r, k) runs phase 1 on (r, k) and
+// phase 2 on (r-1, k-1).
+struct Cursor {
+    int r, k;
+    bool deferred;
 };
 
-// What step u of the strip does: phase 1 on (r1, k1) if has1, phase 2 on (r2, k2) if has2.
-struct StepPlan {
-    int r1, k1, r2, k2;
-    bool has1, has2, row_end, deferred;
-};
-
-__device__ __forceinline__ StepPlan plan_step(const StripCtx &s, int u) {
-    StepPlan p;
-    const int h = s.d->h;
-    if (u < s.nmain) {
-        const int r = s.c0 + u / (s.nk + 1), k = u % (s.nk + 1);
-        p.deferred = false;
-        p.r1 = r;
-        p.k1 = k;
-        p.has1 = (k < s.nk) && (r < s.c1 || s.c1 < h);
-        p.r2 = r - 1;
-        p.k2 = k - 1;
-        p.has2 = (k >= 1) && (r - 1 > s.c0);
-        p.row_end = (k == s.nk);
-    } else {
-        p.deferred = true;
-        p.has1 = false;
-        p.r1 = p.k1 = 0;
-        p.row_end = false;
-        p.r2 = s.c0;
-        p.k2 = u - s.nmain;
-        p.has2 = true;
+__device__ __forceinline__ void advance(Cursor &c, int c1, int nk) {
+    if (c.deferred) {
+        c.k++;
+    } else if (++c.k > nk) {
+        c.k = 0;
+        if (++c.r > c1) {
+            c.deferred = true;
+            c.k = 0;
+        }
     }
-    return p;
 }
 
-// thread 0: stage the phase-1 rows of step u into slot (gs % kStages); a step
-// without phase 1 still arrives once so that every slot phase completes
+// thread 0: stage the phase-1 rows of the step at cursor `c` into slot
+// (gs % kStages); a step without phase 1 still arrives once so that every slot
+// phase completes
 template <int KH, int KW>
-__device__ __forceinline__ void issue_step(const StripCtx &s, int u, uint64_t gs, float *stages, uint64_t *bars) {
+__device__ __forceinline__ void issue_step(const FusedDesc &d, const Cursor &c, int c1, int nk, uint64_t gs,
+                                           float *stages, uint64_t *bars) {
     using G = Geo<KH, KW>;
     const int slot = (int)(gs % kStages);
-    const StepPlan p = plan_step(s, u);
-    const FusedDesc &d = *s.d;
-    if (!p.has1) {
+    const bool has1 = !c.deferred && c.k < nk && (c.r < c1 || c1 < d.h);
+    if (!has1) {
         mbar_arrive_expect_tx(&bars[slot], 0);
         return;
     }
-    const int n1 = min(G::CW, d.w - p.k1 * G::CW);
+    const int n1 = min(G::CW, d.w - c.k * G::CW);
     const uint32_t seg = (uint32_t)(n1 * KW * 4);
     const bool wd = d.hp.wd_on != 0;
     // order this CTA's earlier reads of the slot before the async-proxy writes
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     mbar_arrive_expect_tx(&bars[slot], seg * KH * (wd ? 2u : 1u));
     float *st = stages + (size_t)slot * G::STAGE_FLOATS;
-    const int64_t off = (int64_t)p.r1 * KH * d.W + (int64_t)p.k1 * G::CW * KW;
+    const int64_t off = (int64_t)c.r * KH * d.W + (int64_t)c.k * G::CW * KW;
 #pragma unroll
     for (int i = 0; i < KH; i++) tma_load(st + i * G::ROWF, d.g + off + i * d.W, seg, &bars[slot]);
     if (wd) {
 #pragma unroll
         for (int i = 0; i < KH; i++) tma_load(st + (KH + i) * G::ROWF, d.p + off + i * d.W, seg, &bars[slot]);
+    }
+}
+
+__device__ __forceinline__ void wait_slot(uint64_t *bar, uint64_t gs, int64_t wait_iters, WsHeader *hdr,
+                                          int64_t gstrip) {
+    const uint32_t parity = (uint32_t)((gs / kStages) & 1);
+    int64_t it = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if (++it > wait_iters) {
+            if (threadIdx.x == 0) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
+            break;
+        }
     }
 }
 
@@ -617,14 +616,10 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
                               uint64_t &gstep, WsHeader *hdr, unsigned int *flags, float *halo, int64_t wait_iters) {
     using G = Geo<KH, KW>;
     const int w = d.w, h = d.h;
-    StripCtx s;
-    s.d = &d;
-    s.c0 = sidx * d.L;
-    s.c1 = s.c0 + d.L < h ? s.c0 + d.L : h;
-    s.nk = (w + G::CW - 1) / G::CW;
-    s.nmain = (s.c1 - s.c0 + 1) * (s.nk + 1);
-    s.nsteps = s.nmain + s.nk;
-    const int c0 = s.c0, c1 = s.c1;
+    const int c0 = sidx * d.L;
+    const int c1 = c0 + d.L < h ? c0 + d.L : h;
+    const int nk = (w + G::CW - 1) / G::CW;
+    const int nsteps = (c1 - c0 + 1) * (nk + 1) + nk;
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
     const bool wd = d.hp.wd_on != 0;
     AdamK ak;
@@ -632,28 +627,34 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     ak.rcp_sbc2 = splat(__frcp_rn(d.hp.sqrt_bc2));
     ak.eps = splat(d.hp.eps);
     ak.ns = splat(d.hp.neg_step);
-    auto RR = [&](int c) { return ring + (c % 3) * w; };
     float2 *pub = reinterpret_cast<float2 *>(halo + d.halo_off) + (int64_t)sidx * w;
     // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
     // strip's first row is written at the end
-    auto save_head = [&](int c, int slot) {
-        const float2 *src = RR(c);
+    auto save_head = [&](const float2 *src, int slot) {
         float2 *dst = head + slot * w;
         for (int j = threadIdx.x; j < w; j += kThreads) __stcg(dst + j, src[j]);
     };
 
     // prologue: the first row's state, the first kStages-1 steps' rows
     fetch_row_state(rstate + (c0 & 1) * rstate_stride, d, c0);
+    Cursor ic{c0, 0, false};  // thread 0's issue cursor, kStages-1 steps ahead
     if (threadIdx.x == 0) {
-        for (int u = 0; u < kStages - 1 && u < s.nsteps; u++) issue_step<KH, KW>(s, u, gstep + u, stages, ctl.bar);
+        for (int u = 0; u < kStages - 1 && u < nsteps; u++) {
+            issue_step<KH, KW>(d, ic, c1, nk, gstep + u, stages, ctl.bar);
+            advance(ic, c1, nk);
+        }
     }
     cp_async_wait_all();
     __syncthreads();
 
-    for (int u = 0; u < s.nsteps; u++) {
-        const StepPlan p = plan_step(s, u);
+    Cursor cur{c0, 0, false};
+    // ring rows of the row in phase 1 (r) and its two predecessors
+    float2 *Rm2 = ring + ((c0 + 1) % 3) * w, *Rm1 = ring + ((c0 + 2) % 3) * w, *R0 = ring + (c0 % 3) * w;
+    RowState rs = row_state_view(rstate + (c0 & 1) * rstate_stride, d, c0);
+    for (int u = 0; u < nsteps; u++, advance(cur, c1, nk)) {
         const uint64_t gs = gstep + u;
-        if (p.deferred && u == s.nmain) {
+        const int r = cur.r, k = cur.k;
+        if (cur.deferred && k == 0) {
             // deferred first row: rows c0-1 (the previous strip's published row),
             // c0 and c0+1 go back into ring slots 0, 1, 2
             compute_rowco<KH>(d, c0, ctl.rowco[c0 & 1]);
@@ -673,50 +674,49 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
             __syncthreads();
         }
         // the step kStages-1 ahead goes into the slot the previous step freed
-        if (threadIdx.x == 0 && u + kStages - 1 < s.nsteps)
-            issue_step<KH, KW>(s, u + kStages - 1, gs + kStages - 1, stages, ctl.bar);
-        if (!p.deferred && p.k1 == 0) {
-            if (p.r1 - 1 > c0) compute_rowco<KH>(d, p.r1 - 1, ctl.rowco[(p.r1 - 1) & 1]);
-            // the next row's old state, one row ahead (buffer of row r1-1, done)
-            if (p.r1 + 1 <= c1 && p.r1 + 1 < h)
-                fetch_row_state(rstate + ((p.r1 + 1) & 1) * rstate_stride, d, p.r1 + 1);
+        if (threadIdx.x == 0 && u + kStages - 1 < nsteps) {
+            issue_step<KH, KW>(d, ic, c1, nk, gs + kStages - 1, stages, ctl.bar);
+            advance(ic, c1, nk);
         }
-        P2Regs<KH, KW> pr;
-        if (p.has2) load_p2<KH, KW>(d, p.r2, p.k2, pr);
-        // this step's staged rows
-        {
-            const int slot = (int)(gs % kStages);
-            const uint32_t parity = (uint32_t)((gs / kStages) & 1);
-            int64_t it = 0;
-            while (!mbar_try_wait(&ctl.bar[slot], parity)) {
-                if (++it > wait_iters) {
-                    if (threadIdx.x == 0) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
-                    break;
-                }
+        const bool has1 = !cur.deferred && k < nk && (r < c1 || c1 < h);
+        const bool has2 = cur.deferred || (k >= 1 && r - 1 > c0);
+        if (!cur.deferred && k == 0) {
+            if (r > c0) {
+                // rotate the ring: row r takes the slot of row r-3
+                float2 *t = Rm2;
+                Rm2 = Rm1;
+                Rm1 = R0;
+                R0 = t;
+                rs = row_state_view(rstate + (r & 1) * rstate_stride, d, r);
             }
+            if (r - 1 > c0) compute_rowco<KH>(d, r - 1, ctl.rowco[(r - 1) & 1]);
+            // the next row's old state, one row ahead (the buffer of row r-1, done)
+            if (r + 1 <= c1 && r + 1 < h) fetch_row_state(rstate + ((r + 1) & 1) * rstate_stride, d, r + 1);
         }
-        if (p.has1) {
+        const int pr_row = cur.deferred ? c0 : r - 1;
+        const int pr_k = cur.deferred ? k : k - 1;
+        P2Regs<KH, KW> pr;
+        if (has2) load_p2<KH, KW>(d, pr_row, pr_k, pr);
+        if (has1) {
+            wait_slot(&ctl.bar[gs % kStages], gs, wait_iters, hdr, gstrip);
             const float *stage = stages + (size_t)(gs % kStages) * G::STAGE_FLOATS;
-            const RowState rs = row_state_view(rstate + (p.r1 & 1) * rstate_stride, d, p.r1);
-            if (wd) phase1<KH, KW, true>(d, p.r1, p.k1, stage, rs, RR(p.r1), p.r1 < c1);
-            else phase1<KH, KW, false>(d, p.r1, p.k1, stage, rs, RR(p.r1), p.r1 < c1);
+            if (wd) phase1<KH, KW, true>(d, r, k, stage, rs, R0, r < c1);
+            else phase1<KH, KW, false>(d, r, k, stage, rs, R0, r < c1);
         }
         __syncthreads();
-        if (p.row_end) {
-            const int r = p.r1;
+        if (!cur.deferred && k == nk) {
             if (r < c1) {
-                if (q8) requant_row(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
-                if (r == c0) save_head(r, 0);
-                if (r == c0 + 1) save_head(r, 1);
+                if (q8) requant_row(d, r, R0, r > c0 ? Rm1 : nullptr);
+                if (r == c0) save_head(R0, 0);
+                if (r == c0 + 1) save_head(R0, 1);
                 // the next row's state must have landed before its first chunk
                 cp_async_wait_all();
             } else if (c1 < h) {
                 // look-ahead row done: keep it as the strip's second row if the
                 // strip has one row, then publish this strip's last row for the
                 // next strip (after the look-ahead read of that strip's data)
-                if (r == c0 + 1) save_head(r, 1);
-                const float2 *src = RR(c1 - 1);
-                for (int j = threadIdx.x; j < w; j += kThreads) __stcg(pub + j, src[j]);
+                if (r == c0 + 1) save_head(R0, 1);
+                for (int j = threadIdx.x; j < w; j += kThreads) __stcg(pub + j, Rm1[j]);
                 __syncthreads();
                 if (threadIdx.x == 0) {
                     __threadfence();
@@ -724,20 +724,19 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
                 }
             }
         }
-        if (p.has2) {
-            const int c = p.r2;
-            const RowCo *rc = ctl.rowco[c & 1];
-            if (!p.deferred) {
-                const float2 *R[3] = {RR(c - 1), RR(c), c + 1 < h ? RR(c + 1) : RR(c)};
-                phase2<KH, KW>(d, c, p.k2, R, rc, ak, pr);
+        if (has2) {
+            const RowCo *rc = ctl.rowco[pr_row & 1];
+            if (!cur.deferred) {
+                // phase 2 of row r-1: rows r-2, r-1, r (row r absent past the tensor's end)
+                phase2<KH, KW>(d, r - 1, k - 1, Rm2, Rm1, r < h ? R0 : Rm1, rc, ak, pr);
             } else {
-                const float2 *R[3] = {c0 > 0 ? ring : ring + w, ring + w, c0 + 1 < h ? ring + 2 * w : ring + w};
-                phase2<KH, KW>(d, c, p.k2, R, rc, ak, pr);
+                phase2<KH, KW>(d, c0, k, c0 > 0 ? ring : ring + w, ring + w, c0 + 1 < h ? ring + 2 * w : ring + w,
+                               rc, ak, pr);
             }
         }
         __syncthreads();
     }
-    gstep += (uint64_t)s.nsteps;
+    gstep += (uint64_t)nsteps;
 }
 
 __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s) {
