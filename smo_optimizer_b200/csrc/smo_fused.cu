@@ -1,40 +1,37 @@
 // smo_fused.cu -- fused single-pass step for exact-window pooled tensors.
 //
-// One persistent launch steps every qualifying tensor of a batch.  HBM sees
+// One persistent launch steps every qualifying tensor of the batch.  HBM sees
 // each parameter and gradient element read once and each parameter written
-// once (plus the compact moment state); the parameter values are read a second
-// time from L2.
+// once (plus the compact moment state), instead of the general path's
+// read-pool-write-scratch / read-scratch-interpolate-write round trip.
 //
 // Work unit: a STRIP of L compact rows (KH*L full-resolution rows), full
 // width, of one tensor.  CTAs take strips in increasing order from an atomic
-// counter in the workspace header.  A strip is walked as a sequence of STEPS:
-// compact row r is split into column chunks of CW compact cells, and step
-// (r, k) does
+// counter in the workspace header.  Inside a strip the CTA runs a row pipeline
+// over compact rows c:
 //
-//   phase 1 (row r, chunk k)     window sums of x = g + wd*p and x*x, dequant of
-//                                the old codes, EMA; post-EMA (m, v) pairs go to
-//                                a 3-row ring in shared memory;
-//   phase 2 (row r-1, chunk k-1) bilinear reconstruction (width pass, then
-//                                height pass, torch's order) and the Adam write
-//                                of the KH parameter rows of that chunk.
-//
-// The gradient and parameter rows that phase 1 of a step reads are brought
-// into a shared-memory stage by TMA bulk copies (cp.async.bulk, completion on
-// an mbarrier) kStages-1 steps ahead, issued by one thread; the codes, scales
-// or fp32 state of a row arrive by cp.async one row ahead; the parameter values
-// phase 2 rewrites are loaded into registers at the start of the step.  When a
-// row's last chunk is done its int8 blocks are requantised.
+//   phase 1 (row c)   window sums of x = g + wd*p and x*x (KH x KW windows,
+//                     vector loads), dequant of the old codes, EMA; post-EMA
+//                     fp32 m, v of the row go to a 3-row ring in shared memory;
+//                     int8 blocks completed by this row are requantised and
+//                     written (POOLED32: the new fp32 state is written).
+//   phase 2 (row c-1) bilinear reconstruction of m, v from ring rows c-2..c
+//                     (width pass, then height pass, torch's order), clamp,
+//                     Adam write of the KH parameter rows.
 //
 // Neighbouring strips: the write of a strip's last row needs the first row of
 // the next strip.  The CTA recomputes that row itself (look-ahead) from the
-// next strip's g, p and OLD moment state; the old state is intact because the
-// moments are double-buffered (read *_in, write *_out).  The write of a
+// next strip's g, p and OLD moment state; the old state is intact because
+// the moments are double-buffered (read *_in, write *_out).  The write of a
 // strip's FIRST row needs the previous strip's last row, which the previous
 // strip publishes to the workspace (with a release flag) after its look-ahead
 // read; so the first row is written last, after an acquire wait.  Waits only
 // ever point at an earlier strip, which some running CTA took before this one,
 // so they cannot deadlock whatever the residency; every wait is bounded and
 // reports SMO_ERR_TIMEOUT in the workspace header instead of hanging.
+//
+// The parameter rows read in phase 1 are read again in phase 2 one pipeline
+// step later; that second read is meant to hit L2.
 #include <cstdlib>
 #include <cstring>
 #include <vector>
@@ -44,32 +41,16 @@
 
 namespace smo {
 
-constexpr int kThreads = 256;
-constexpr int kStages = 4;                  // shared-memory stages (kStages-1 steps of look-ahead)
-constexpr int kMaxFusedCtasPerSm = 2;
+constexpr int kFusedThreads = 256;
+constexpr int kMaxFusedCtasPerSm = 4;
 constexpr int kMaxFused = 104;
 constexpr int64_t kStripRows = 16;          // target compact rows per strip
-constexpr int64_t kMaxFusedCols = 4096;     // compact columns per tensor
+constexpr int64_t kMaxFusedCols = 8192;     // compact columns (shared memory: 24 B per column)
 constexpr int64_t kDefaultWaitIters = 1 << 22;
 
-// Chunk geometry of a KH x KW window: CW compact cells per step (one per
-// phase-1 thread); in phase 2 TPC threads share a cell, RPT rows each.
-template <int KH, int KW>
-struct Geo {
-    static constexpr int CW = (2048 / (KH * KW)) > kThreads ? kThreads : 2048 / (KH * KW);
-    static constexpr int TPC = kThreads / CW;
-    static constexpr int RPT = KH / TPC;
-    static constexpr int ROWF = CW * KW;               // floats of one staged full-resolution row
-    static constexpr int STAGE_FLOATS = 2 * KH * ROWF; // gradient rows, then parameter rows
-    // ring rows one thread's output rows draw on: two when its rows lie in one
-    // half of the window, all three when they cover both halves
-    static constexpr int NR = (RPT > KH / 2) ? 3 : 2;
-    static_assert(RPT >= 1 && TPC * RPT == KH, "phase-2 mapping");
-};
-
 // n / d for 32-bit unsigned n by a divisor fixed per tensor: multiply by a
-// precomputed magic number (Granlund-Montgomery / Hacker's Delight 10-1, the
-// round-up variant with a 33-bit add), set up on the host.
+// precomputed magic number (Granlund-Montgomery / Hacker's Delight 10-1,
+// the round-up variant with a 33-bit add), set up on the host.
 struct FastDiv {
     uint32_t d, m, l;
 };
@@ -98,6 +79,7 @@ struct FusedDesc {
     int64_t halo_off;  // float offset of this tensor's published rows in the halo area
     int32_t h, w, B, L;
     FastDiv div_B;     // cell -> quant block
+    FastDiv div_w;     // cell -> compact row
     int32_t kind;
     smo_hyper hp;
 };
@@ -109,49 +91,50 @@ struct FusedBatch {
 };
 static_assert(sizeof(FusedBatch) < 30000, "kernel parameter batch must stay below 32 KB");
 
-// ---------------------------------------------------------------- async copies
+// ---------------------------------------------------------------- memory helpers
 
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+template <int KW>
+__device__ __forceinline__ void load_grad_row(const float *ptr, float (&v)[KW]) {
+    if constexpr (KW % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < KW / 4; k++) {
+            float4 t = __ldcs(reinterpret_cast<const float4 *>(ptr) + k);
+            v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+        }
+    } else {
+        static_assert(KW == 2, "window width");
+        float2 t = __ldcs(reinterpret_cast<const float2 *>(ptr));
+        v[0] = t.x; v[1] = t.y;
+    }
 }
 
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
+// parameter loads: L2-cached (phase 1, re-read one pipeline step later) or last use (phase 2)
+template <int KW, bool kLastUse>
+__device__ __forceinline__ void load_param_row(const float *ptr, float (&v)[KW]) {
+    if constexpr (KW % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < KW / 4; k++) {
+            const float4 *q = reinterpret_cast<const float4 *>(ptr) + k;
+            float4 t = kLastUse ? __ldlu(q) : __ldcg(q);
+            v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
+        }
+    } else {
+        const float2 *q = reinterpret_cast<const float2 *>(ptr);
+        float2 t = kLastUse ? __ldlu(q) : __ldcg(q);
+        v[0] = t.x; v[1] = t.y;
+    }
 }
 
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
-    uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return done != 0;
+template <int KW>
+__device__ __forceinline__ void store_param_row(float *ptr, const float (&v)[KW]) {
+    if constexpr (KW % 4 == 0) {
+#pragma unroll
+        for (int k = 0; k < KW / 4; k++)
+            __stcs(reinterpret_cast<float4 *>(ptr) + k, make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]));
+    } else {
+        __stcs(reinterpret_cast<float2 *>(ptr), make_float2(v[0], v[1]));
+    }
 }
-
-// 1-D TMA bulk copy global -> shared, completion counted on `bar` (both
-// addresses 16-byte aligned, bytes a multiple of 16)
-__device__ __forceinline__ void tma_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void store_release(unsigned int *flag, unsigned int v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
@@ -198,6 +181,7 @@ __device__ __forceinline__ float div_rcp(float x, float c, float r) {
     return fabsf(x) == __int_as_float(0x7f800000) ? x : q;
 }
 
+// the same for a pair, with per-lane constants (c.x, c.y) and reciprocals
 __device__ __forceinline__ float2 div_rcp2(float2 x, float2 c, float2 r) {
     const float2 q0 = __fmul2_rn(x, r);
     const float2 rem = __ffma2_rn(q0, f2(-c.x, -c.y), x);
@@ -245,65 +229,17 @@ __device__ __forceinline__ int8_t quantize_rc(float x, float s, float rs) {
     return (r == r) ? (int8_t)(int)r : (int8_t)0;
 }
 
-// ---------------------------------------------------------------- row state
-//
-// The moment state phase 1 reads for one compact row, staged by cp.async one
-// row ahead: POOLED8: m codes [w] int8, v codes [w] int8, m scales and v
-// scales of the blocks the row touches; POOLED32: m [w], v [w] fp32.
-
-struct RowState {
-    const int8_t *mq, *vq;
-    const float *ms, *vs;
-    const float *m, *v;
-    uint32_t b0;  // first block of the row (POOLED8)
-};
-
-__device__ __forceinline__ RowState row_state_view(char *base, const FusedDesc &d, int r) {
-    RowState s;
-    const int w = d.w;
-    if (d.kind == SMO_KIND_POOLED8) {
-        const uint32_t first = fast_div((uint32_t)r * (uint32_t)w, d.div_B);
-        const uint32_t last = fast_div(((uint32_t)r + 1u) * (uint32_t)w - 1u, d.div_B);
-        s.mq = (const int8_t *)base;
-        s.vq = (const int8_t *)base + w;
-        s.ms = (const float *)(base + 2 * w);
-        s.vs = s.ms + (last - first + 1);
-        s.b0 = first;
-        s.m = s.v = nullptr;
-    } else {
-        s.m = (const float *)base;
-        s.v = (const float *)base + w;
-        s.mq = s.vq = nullptr;
-        s.ms = s.vs = nullptr;
-        s.b0 = 0;
-    }
-    return s;
-}
-
-// all threads: issue the cp.async copies of row r's old state (w % 16 == 0)
-__device__ __forceinline__ void fetch_row_state(char *base, const FusedDesc &d, int r) {
-    const int w = d.w;
-    const int64_t off = (int64_t)r * w;
-    if (d.kind == SMO_KIND_POOLED8) {
-        const uint32_t first = fast_div((uint32_t)r * (uint32_t)w, d.div_B);
-        const uint32_t last = fast_div(((uint32_t)r + 1u) * (uint32_t)w - 1u, d.div_B);
-        const int nb = (int)(last - first + 1);
-        int8_t *mq = (int8_t *)base, *vq = (int8_t *)base + w;
-        float *ms = (float *)(base + 2 * w), *vs = ms + nb;
-        for (int i = threadIdx.x; i < w / 16; i += kThreads) {
-            cp_async16(mq + 16 * i, d.mq_in + off + 16 * i);
-            cp_async16(vq + 16 * i, d.vq_in + off + 16 * i);
-        }
-        for (int i = threadIdx.x; i < nb; i += kThreads) {
-            cp_async4(ms + i, d.ms_in + first + i);
-            cp_async4(vs + i, d.vs_in + first + i);
-        }
-    } else {
-        float *m = (float *)base, *v = (float *)base + w;
-        for (int i = threadIdx.x; i < w / 4; i += kThreads) {
-            cp_async16(m + 4 * i, d.m_in + off + 4 * i);
-            cp_async16(v + 4 * i, d.v_in + off + 4 * i);
-        }
+// Hint the next compact row's gradient and parameter rows into L2 (TMA bulk
+// prefetch; no shared memory, no completion to wait for).
+template <int KH>
+__device__ __forceinline__ void prefetch_row_l2(const FusedDesc &d, int c) {
+    const int i = threadIdx.x;
+    if (i < 2 * KH) {
+        const float *base = (i < KH ? d.g : d.p) + ((int64_t)c * KH + (i % KH)) * d.W;
+        if (i >= KH && !d.hp.wd_on) return;
+        const uint32_t bytes = (uint32_t)((d.W * 4) & ~(int64_t)15);
+        if (((uintptr_t)base & 15) == 0 && bytes > 0)
+            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(bytes) : "memory");
     }
 }
 
@@ -312,32 +248,13 @@ __device__ __forceinline__ void fetch_row_state(char *base, const FusedDesc &d, 
 // (sum x, sum x*x) of one KH x KW window in row-major order from +0, times
 // 1/(KH*KW) (a power of two: the same value as avg_pool2d's division)
 template <int KH, int KW, bool WD>
-__device__ __forceinline__ float2 pool_cell(const float *sg, const float *sp, float wd) {
+__device__ __forceinline__ float2 pool_cell(const float (&gv)[KH][KW], const float (&pv)[KH][KW], float wd) {
     float2 acc = f2(0.0f, 0.0f);
 #pragma unroll
     for (int i = 0; i < KH; i++) {
-        float gv[KW], pv[KW];
-#pragma unroll
-        for (int k = 0; k < KW; k += (KW >= 4 ? 4 : 2)) {
-            if constexpr (KW >= 4) {
-                const float4 t = *reinterpret_cast<const float4 *>(sg + i * Geo<KH, KW>::ROWF + k);
-                gv[k] = t.x; gv[k + 1] = t.y; gv[k + 2] = t.z; gv[k + 3] = t.w;
-                if (WD) {
-                    const float4 u = *reinterpret_cast<const float4 *>(sp + i * Geo<KH, KW>::ROWF + k);
-                    pv[k] = u.x; pv[k + 1] = u.y; pv[k + 2] = u.z; pv[k + 3] = u.w;
-                }
-            } else {
-                const float2 t = *reinterpret_cast<const float2 *>(sg + i * Geo<KH, KW>::ROWF + k);
-                gv[k] = t.x; gv[k + 1] = t.y;
-                if (WD) {
-                    const float2 u = *reinterpret_cast<const float2 *>(sp + i * Geo<KH, KW>::ROWF + k);
-                    pv[k] = u.x; pv[k + 1] = u.y;
-                }
-            }
-        }
 #pragma unroll
         for (int k = 0; k < KW; k++) {
-            const float x = WD ? __fmaf_rn(wd, pv[k], gv[k]) : gv[k];
+            const float x = WD ? __fmaf_rn(wd, pv[i][k], gv[i][k]) : gv[i][k];
             acc = __fadd2_rn(acc, f2(x, __fmul_rn(x, x)));
         }
     }
@@ -345,32 +262,62 @@ __device__ __forceinline__ float2 pool_cell(const float *sg, const float *sp, fl
     return __fmul2_rn(acc, splat(inv));
 }
 
-// Phase 1 of (row r, chunk k): thread j < n1 owns compact cell k*CW + j.
-template <int KH, int KW, bool WD>
-__device__ __forceinline__ void phase1(const FusedDesc &d, int r, int k, const float *stage, const RowState &rs,
-                                       float2 *ringrow, bool own) {
-    using G = Geo<KH, KW>;
-    const int j = threadIdx.x;
-    const int n1 = min(G::CW, d.w - k * G::CW);
-    if (j >= n1) return;
-    const int col = k * G::CW + j;
-    const float2 pooled = pool_cell<KH, KW, WD>(stage + j * KW, stage + KH * G::ROWF + j * KW, d.hp.weight_decay);
+// dequant of the old moments, EMA, post-EMA pair into the ring row
+__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, float2 pooled, float2 *row, int j,
+                                         bool own) {
     const smo_hyper &hp = d.hp;
     float2 mv;
     if (d.kind == SMO_KIND_POOLED8) {
-        const uint32_t cell = (uint32_t)r * (uint32_t)d.w + (uint32_t)col;
-        const uint32_t bi = fast_div(cell, d.div_B) - rs.b0;
-        mv = dequant2(rs.mq[col], rs.vq[col], rs.ms[bi], rs.vs[bi]);
+        const uint32_t b = fast_div(cell, d.div_B);
+        mv = dequant2(d.mq_in[cell], d.vq_in[cell], d.ms_in[b], d.vs_in[b]);
     } else {
-        mv = f2(rs.m[col], rs.v[col]);
+        mv = f2(d.m_in[cell], d.v_in[cell]);
     }
     mv = __ffma2_rn(f2(hp.omb1, hp.omb2), pooled, __fmul2_rn(mv, f2(hp.beta1, hp.beta2)));
-    ringrow[col] = mv;
+    row[j] = mv;
     if (own && d.kind == SMO_KIND_POOLED32) {
-        const int64_t cell = (int64_t)r * d.w + col;
         d.m_out[cell] = mv.x;
         d.v_out[cell] = mv.y;
     }
+}
+
+// Phase 1 of compact row c: post-EMA (m, v) into `row` (shared memory).
+// `own` rows also write the fp32 state (POOLED32); look-ahead rows only read.
+// CELLS cells per thread per iteration keep CELLS*KH*KW*2 loads in flight.
+template <int KH, int KW, int CELLS, bool WD>
+__device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row, bool own) {
+    const int w = d.w;
+    const int64_t W = d.W;
+    const float *gb = d.g + (int64_t)c * KH * W;
+    const float *pb = d.p + (int64_t)c * KH * W;
+    const uint32_t cell0 = (uint32_t)c * (uint32_t)w;
+    const float wd = d.hp.weight_decay;
+    for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * kFusedThreads) {
+        float gv[CELLS][KH][KW], pv[CELLS][KH][KW];
+#pragma unroll
+        for (int u = 0; u < CELLS; u++) {
+            const int j = j0 + u * kFusedThreads;
+            if (u == 0 || j < w) {
+#pragma unroll
+                for (int i = 0; i < KH; i++) load_grad_row<KW>(gb + i * W + (int64_t)j * KW, gv[u][i]);
+                if (WD) {
+#pragma unroll
+                    for (int i = 0; i < KH; i++) load_param_row<KW, false>(pb + i * W + (int64_t)j * KW, pv[u][i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < CELLS; u++) {
+            const int j = j0 + u * kFusedThreads;
+            if (u == 0 || j < w) ema_cell(d, cell0 + j, pool_cell<KH, KW, WD>(gv[u], pv[u], wd), row, j, own);
+        }
+    }
+}
+
+template <int KH, int KW, int CELLS>
+__device__ __forceinline__ void phase1(const FusedDesc &d, int c, float2 *row, bool own) {
+    if (d.hp.wd_on) phase1_wd<KH, KW, CELLS, true>(d, c, row, own);
+    else phase1_wd<KH, KW, CELLS, false>(d, c, row, own);
 }
 
 // Requantise the int8 blocks that compact row c completes.  A block spans at
@@ -409,7 +356,7 @@ __device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const flo
     uint32_t b_hi = fast_div(((uint32_t)c + 1u) * w, d.div_B);
     if (c == d.h - 1 && C % B != 0) b_hi = C / B + 1;  // the zero-padded last block
     const bool aligned = (w % B) == 0;                  // blocks never leave the row
-    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += kThreads / 32)
+    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += kFusedThreads / 32)
         requant_block(d, b, c, Rc, Rp, aligned);
 }
 
@@ -440,303 +387,149 @@ __device__ __forceinline__ float col_l1(int t) {
     return (t + 0.5f) / KW + (t < KW / 2 ? 0.5f : -0.5f);
 }
 
-// Parameter values phase 2 of a step rewrites, loaded into registers at the
-// start of the step (L2 hits: phase 1 of the same row read them).
+// Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
+// c-1 (R[0]), c (R[1]), c+1 (R[2]) in shared memory (an absent neighbour row
+// is passed as row c and never weighted).  Row weights come from `rowco`.
 template <int KH, int KW>
-struct P2Regs {
-    float v[Geo<KH, KW>::RPT][KW];
-};
-
-template <int KH, int KW>
-__device__ __forceinline__ void load_p2(const FusedDesc &d, int c, int k, P2Regs<KH, KW> &pr) {
-    using G = Geo<KH, KW>;
-    const int j = threadIdx.x % G::CW;
-    const int i0 = (threadIdx.x / G::CW) * G::RPT;
-    const int n = min(G::CW, d.w - k * G::CW);
-    if (j >= n) return;
-    const float *base = d.p + ((int64_t)c * KH + i0) * d.W + (int64_t)(k * G::CW + j) * KW;
-#pragma unroll
-    for (int i = 0; i < G::RPT; i++) {
-#pragma unroll
-        for (int t = 0; t < KW; t += 2) {
-            const float2 x = __ldcg(reinterpret_cast<const float2 *>(base + i * d.W + t));
-            pr.v[i][t] = x.x;
-            pr.v[i][t + 1] = x.y;
-        }
-    }
-}
-
-// Phase 2 of (row c, chunk k): the thread's RPT output rows of cell k*CW + j,
-// from the post-EMA rows c-1 (R0), c (R1), c+1 (R2) (an absent neighbour row is
-// passed as row c and never weighted); row weights from `rowco`.
-template <int KH, int KW>
-__device__ __forceinline__ void phase2(const FusedDesc &d, int c, int k, const float2 *R0, const float2 *R1,
-                                       const float2 *R2, const RowCo *rowco, const AdamK &ak,
-                                       const P2Regs<KH, KW> &pr) {
-    using G = Geo<KH, KW>;
-    constexpr int NR = G::NR;
-    const int j = threadIdx.x % G::CW;
-    const int i0 = (threadIdx.x / G::CW) * G::RPT;
+__device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
+                                       const AdamK &ak) {
     const int w = d.w;
-    const int n = min(G::CW, w - k * G::CW);
-    if (j >= n) return;
-    const int col = k * G::CW + j;
-    // the ring rows the thread's output rows draw on: sa .. sa+NR-1
-    int sa = 0;
-    if (NR == 2) {
-        sa = 2;
+    const int64_t W = d.W;
+    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+        float *pbase = d.p + (int64_t)c * KH * W + (int64_t)j * KW;
+        float pv[KH][KW];
 #pragma unroll
-        for (int i = 0; i < G::RPT; i++) sa = min(sa, rowco[i0 + i].s0);
-        sa = min(sa, 1);
-    }
-    // width pass: the left half of the window interpolates columns (col-1, col),
-    // the right half (col, col+1), clamped at the edges exactly as torch does
-    const int jr = col + 1 < w ? col + 1 : w - 1;
-    const int la = col > 0 ? col - 1 : 0;
-    float2 hw[NR][KW];
+        for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
+        // width pass of the three compact rows: the left half of the window
+        // interpolates columns (j-1, j), the right half (j, j+1), clamped at the
+        // edges exactly as torch's index/lambda computation does
+        const int jr = j + 1 < w ? j + 1 : w - 1;
+        const int la = j > 0 ? j - 1 : 0;
+        float2 h[3][KW];
 #pragma unroll
-    for (int q = 0; q < NR; q++) {
-        const int sr = sa + q;
-        const float2 *row = sr == 0 ? R0 : (sr == 1 ? R1 : R2);
-        const float2 L = row[la], M = row[col], Rr = row[jr];
-        const float2 X = col > 0 ? M : Rr;
+        for (int s = 0; s < 3; s++) {
+            const float2 left = R[s][la], mid = R[s][j], right = R[s][jr];
+            const float2 x = j > 0 ? mid : right;
 #pragma unroll
-        for (int t = 0; t < KW; t++) {
-            if (t < KW / 2) {
-                const float l1 = col > 0 ? col_l1<KW>(t) : 0.0f;
-                const float l0 = col > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
-                hw[q][t] = __ffma2_rn(L, splat(l0), __fmul2_rn(X, splat(l1)));
-            } else {
-                hw[q][t] = __ffma2_rn(M, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(Rr, splat(col_l1<KW>(t))));
-            }
-        }
-    }
-    float *base = d.p + ((int64_t)c * KH + i0) * d.W + (int64_t)col * KW;
-#pragma unroll
-    for (int i = 0; i < G::RPT; i++) {
-        const RowCo rc = rowco[i0 + i];
-        const int qa = rc.s0 - sa, qb = rc.s1 - sa;
-#pragma unroll
-        for (int t = 0; t < KW; t += 2) {
-            float2 mh[2];
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                float2 x, y;
-                if (NR == 2) {
-                    x = qa == 0 ? hw[0][t + u] : hw[NR - 1][t + u];
-                    y = qb == 0 ? hw[0][t + u] : hw[NR - 1][t + u];
+            for (int t = 0; t < KW; t++) {
+                if (t < KW / 2) {
+                    const float l1 = j > 0 ? col_l1<KW>(t) : 0.0f;
+                    const float l0 = j > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
+                    h[s][t] = __ffma2_rn(left, splat(l0), __fmul2_rn(x, splat(l1)));
                 } else {
-                    x = qa == 0 ? hw[0][t + u] : (qa == 1 ? hw[1][t + u] : hw[NR - 1][t + u]);
-                    y = qb == 0 ? hw[0][t + u] : (qb == 1 ? hw[1][t + u] : hw[NR - 1][t + u]);
+                    h[s][t] = __ffma2_rn(mid, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(right, splat(col_l1<KW>(t))));
                 }
-                mh[u] = __ffma2_rn(x, splat(rc.l0), __fmul2_rn(y, splat(rc.l1)));
             }
-            const float2 pn = adam_write2(f2(pr.v[i][t], pr.v[i][t + 1]), f2(mh[0].x, mh[1].x),
-                                          f2(clamp_min0(mh[0].y), clamp_min0(mh[1].y)), ak);
-            __stcs(reinterpret_cast<float2 *>(base + i * d.W + t), pn);
         }
-    }
-}
-
-// ---------------------------------------------------------------- strip driver
-
-struct SharedCtl {
-    uint64_t bar[kStages];
-    RowCo rowco[2][8];
-    int64_t strip;
-    unsigned int epoch;
-    int ok;
-};
-
-// Step cursor of a strip: main steps walk rows c0..c1 (c1 = the look-ahead
-// row, or one past the tensor's last row), chunks 0..nk each; then nk deferred
-// steps rewrite the strip's first row.  Step (r, k) runs phase 1 on (r, k) and
-// phase 2 on (r-1, k-1).
-struct Cursor {
-    int r, k;
-    bool deferred;
-};
-
-__device__ __forceinline__ void advance(Cursor &c, int c1, int nk) {
-    if (c.deferred) {
-        c.k++;
-    } else if (++c.k > nk) {
-        c.k = 0;
-        if (++c.r > c1) {
-            c.deferred = true;
-            c.k = 0;
-        }
-    }
-}
-
-// thread 0: stage the phase-1 rows of the step at cursor `c` into slot
-// (gs % kStages); a step without phase 1 still arrives once so that every slot
-// phase completes
-template <int KH, int KW>
-__device__ __forceinline__ void issue_step(const FusedDesc &d, const Cursor &c, int c1, int nk, uint64_t gs,
-                                           float *stages, uint64_t *bars) {
-    using G = Geo<KH, KW>;
-    const int slot = (int)(gs % kStages);
-    const bool has1 = !c.deferred && c.k < nk && (c.r < c1 || c1 < d.h);
-    if (!has1) {
-        mbar_arrive_expect_tx(&bars[slot], 0);
-        return;
-    }
-    const int n1 = min(G::CW, d.w - c.k * G::CW);
-    const uint32_t seg = (uint32_t)(n1 * KW * 4);
-    const bool wd = d.hp.wd_on != 0;
-    // order this CTA's earlier reads of the slot before the async-proxy writes
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    mbar_arrive_expect_tx(&bars[slot], seg * KH * (wd ? 2u : 1u));
-    float *st = stages + (size_t)slot * G::STAGE_FLOATS;
-    const int64_t off = (int64_t)c.r * KH * d.W + (int64_t)c.k * G::CW * KW;
 #pragma unroll
-    for (int i = 0; i < KH; i++) tma_load(st + i * G::ROWF, d.g + off + i * d.W, seg, &bars[slot]);
-    if (wd) {
+        for (int i = 0; i < KH; i++) {
+            const RowCo rc = rowco[i];
+            const bool lo0 = rc.s0 == 0, lo1 = rc.s1 == 1;  // uniform across the CTA
+            float2 mh[KW];
 #pragma unroll
-        for (int i = 0; i < KH; i++) tma_load(st + (KH + i) * G::ROWF, d.p + off + i * d.W, seg, &bars[slot]);
-    }
-}
-
-__device__ __forceinline__ void wait_slot(uint64_t *bar, uint64_t gs, int64_t wait_iters, WsHeader *hdr,
-                                          int64_t gstrip) {
-    const uint32_t parity = (uint32_t)((gs / kStages) & 1);
-    int64_t it = 0;
-    while (!mbar_try_wait(bar, parity)) {
-        if (++it > wait_iters) {
-            if (threadIdx.x == 0) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
-            break;
+            for (int t = 0; t < KW; t++) {
+                const float2 a = lo0 ? h[0][t] : h[1][t];
+                const float2 b = lo1 ? h[1][t] : h[2][t];
+                mh[t] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
+            }
+#pragma unroll
+            for (int t = 0; t < KW; t += 2) {
+                const float2 pn = adam_write2(f2(pv[i][t], pv[i][t + 1]), f2(mh[t].x, mh[t + 1].x),
+                                              f2(clamp_min0(mh[t].y), clamp_min0(mh[t + 1].y)), ak);
+                pv[i][t] = pn.x;
+                pv[i][t + 1] = pn.y;
+            }
+            store_param_row<KW>(pbase + i * W, pv[i]);
         }
     }
 }
 
-template <int KH, int KW>
-__device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float *stages,
-                              float2 *ring, char *rstate, int rstate_stride, float2 *head, SharedCtl &ctl,
-                              uint64_t &gstep, WsHeader *hdr, unsigned int *flags, float *halo, int64_t wait_iters) {
-    using G = Geo<KH, KW>;
+// One strip: phase-1 rows r = c0 .. c1 (c1 = look-ahead row, when it exists),
+// each followed by phase 2 of row r-1; then the strip's first row.
+template <int KH, int KW, int CELLS>
+__device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float2 *ring,
+                              float2 *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
+                              int64_t wait_iters) {
     const int w = d.w, h = d.h;
     const int c0 = sidx * d.L;
     const int c1 = c0 + d.L < h ? c0 + d.L : h;
-    const int nk = (w + G::CW - 1) / G::CW;
-    const int nsteps = (c1 - c0 + 1) * (nk + 1) + nk;
+    const int last = c1 < h ? c1 : c1 - 1;  // last phase-1 row
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
-    const bool wd = d.hp.wd_on != 0;
     AdamK ak;
     ak.sbc2 = splat(d.hp.sqrt_bc2);
     ak.rcp_sbc2 = splat(__frcp_rn(d.hp.sqrt_bc2));
     ak.eps = splat(d.hp.eps);
     ak.ns = splat(d.hp.neg_step);
+    auto RR = [&](int c) { return ring + (c % 3) * w; };
     float2 *pub = reinterpret_cast<float2 *>(halo + d.halo_off) + (int64_t)sidx * w;
     // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
     // strip's first row is written at the end
-    auto save_head = [&](const float2 *src, int slot) {
+    auto save_head = [&](int c, int slot) {
+        const float2 *src = RR(c);
         float2 *dst = head + slot * w;
-        for (int j = threadIdx.x; j < w; j += kThreads) __stcg(dst + j, src[j]);
+        for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(dst + j, src[j]);
     };
 
-    // prologue: the first row's state, the first kStages-1 steps' rows
-    fetch_row_state(rstate + (c0 & 1) * rstate_stride, d, c0);
-    Cursor ic{c0, 0, false};  // thread 0's issue cursor, kStages-1 steps ahead
-    if (threadIdx.x == 0) {
-        for (int u = 0; u < kStages - 1 && u < nsteps; u++) {
-            issue_step<KH, KW>(d, ic, c1, nk, gstep + u, stages, ctl.bar);
-            advance(ic, c1, nk);
+    for (int r = c0; r <= last; r++) {
+        const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
+        if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
+        if (r < last) prefetch_row_l2<KH>(d, r + 1);
+        phase1<KH, KW, CELLS>(d, r, RR(r), r < c1);
+        __syncthreads();
+        if (r < c1) {
+            if (q8) requant_row(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
+            if (r == c0) save_head(r, 0);
+            if (r == c0 + 1) save_head(r, 1);
+        } else {
+            // look-ahead row: keep it as the strip's second row if the strip has
+            // one row, then publish this strip's last row for the next strip
+            // (after the look-ahead read of that strip's parameters and state)
+            if (r == c0 + 1) save_head(r, 1);
+            const float2 *src = RR(c1 - 1);
+            for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(pub + j, src[j]);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                __threadfence();
+                store_release(flags + gstrip, epoch);
+            }
         }
+        if (do2) {
+            const float2 *R[3] = {RR(r - 2), RR(r - 1), RR(r)};
+            phase2<KH, KW>(d, r - 1, R, rowco[(r - 1) & 1], ak);
+        }
+        __syncthreads();
     }
-    cp_async_wait_all();
-    __syncthreads();
+    if (c1 == h && c1 - 1 > c0) {
+        // the tensor's last row: no look-ahead row below it
+        compute_rowco<KH>(d, c1 - 1, rowco[(c1 - 1) & 1]);
+        __syncthreads();
+        const float2 *R[3] = {RR(c1 - 2), RR(c1 - 1), RR(c1 - 1)};
+        phase2<KH, KW>(d, c1 - 1, R, rowco[(c1 - 1) & 1], ak);
+        __syncthreads();
+    }
 
-    Cursor cur{c0, 0, false};
-    // ring rows of the row in phase 1 (r) and its two predecessors
-    float2 *Rm2 = ring + ((c0 + 1) % 3) * w, *Rm1 = ring + ((c0 + 2) % 3) * w, *R0 = ring + (c0 % 3) * w;
-    RowState rs = row_state_view(rstate + (c0 & 1) * rstate_stride, d, c0);
-    for (int u = 0; u < nsteps; u++, advance(cur, c1, nk)) {
-        const uint64_t gs = gstep + u;
-        const int r = cur.r, k = cur.k;
-        if (cur.deferred && k == 0) {
-            // deferred first row: rows c0-1 (the previous strip's published row),
-            // c0 and c0+1 go back into ring slots 0, 1, 2
-            compute_rowco<KH>(d, c0, ctl.rowco[c0 & 1]);
-            if (c0 > 0 && threadIdx.x == 0) {
-                const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
-                if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
-                ctl.ok = ok;
-            }
-            __syncthreads();
-            const float2 *prev = pub - (sidx > 0 ? w : 0);
-            const bool ok = c0 > 0 && ctl.ok;
-            for (int j = threadIdx.x; j < w; j += kThreads) {
-                if (c0 > 0) ring[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
-                ring[w + j] = __ldcg(head + j);
-                if (c0 + 1 < h) ring[2 * w + j] = __ldcg(head + w + j);
-            }
-            __syncthreads();
-        }
-        // the step kStages-1 ahead goes into the slot the previous step freed
-        if (threadIdx.x == 0 && u + kStages - 1 < nsteps) {
-            issue_step<KH, KW>(d, ic, c1, nk, gs + kStages - 1, stages, ctl.bar);
-            advance(ic, c1, nk);
-        }
-        const bool has1 = !cur.deferred && k < nk && (r < c1 || c1 < h);
-        const bool has2 = cur.deferred || (k >= 1 && r - 1 > c0);
-        if (!cur.deferred && k == 0) {
-            if (r > c0) {
-                // rotate the ring: row r takes the slot of row r-3
-                float2 *t = Rm2;
-                Rm2 = Rm1;
-                Rm1 = R0;
-                R0 = t;
-                rs = row_state_view(rstate + (r & 1) * rstate_stride, d, r);
-            }
-            if (r - 1 > c0) compute_rowco<KH>(d, r - 1, ctl.rowco[(r - 1) & 1]);
-            // the next row's old state, one row ahead (the buffer of row r-1, done)
-            if (r + 1 <= c1 && r + 1 < h) fetch_row_state(rstate + ((r + 1) & 1) * rstate_stride, d, r + 1);
-        }
-        const int pr_row = cur.deferred ? c0 : r - 1;
-        const int pr_k = cur.deferred ? k : k - 1;
-        P2Regs<KH, KW> pr;
-        if (has2) load_p2<KH, KW>(d, pr_row, pr_k, pr);
-        if (has1) {
-            wait_slot(&ctl.bar[gs % kStages], gs, wait_iters, hdr, gstrip);
-            const float *stage = stages + (size_t)(gs % kStages) * G::STAGE_FLOATS;
-            if (wd) phase1<KH, KW, true>(d, r, k, stage, rs, R0, r < c1);
-            else phase1<KH, KW, false>(d, r, k, stage, rs, R0, r < c1);
-        }
-        __syncthreads();
-        if (!cur.deferred && k == nk) {
-            if (r < c1) {
-                if (q8) requant_row(d, r, R0, r > c0 ? Rm1 : nullptr);
-                if (r == c0) save_head(R0, 0);
-                if (r == c0 + 1) save_head(R0, 1);
-                // the next row's state must have landed before its first chunk
-                cp_async_wait_all();
-            } else if (c1 < h) {
-                // look-ahead row done: keep it as the strip's second row if the
-                // strip has one row, then publish this strip's last row for the
-                // next strip (after the look-ahead read of that strip's data)
-                if (r == c0 + 1) save_head(R0, 1);
-                for (int j = threadIdx.x; j < w; j += kThreads) __stcg(pub + j, Rm1[j]);
-                __syncthreads();
-                if (threadIdx.x == 0) {
-                    __threadfence();
-                    store_release(flags + gstrip, epoch);
-                }
-            }
-        }
-        if (has2) {
-            const RowCo *rc = ctl.rowco[pr_row & 1];
-            if (!cur.deferred) {
-                // phase 2 of row r-1: rows r-2, r-1, r (row r absent past the tensor's end)
-                phase2<KH, KW>(d, r - 1, k - 1, Rm2, Rm1, r < h ? R0 : Rm1, rc, ak, pr);
-            } else {
-                phase2<KH, KW>(d, c0, k, c0 > 0 ? ring : ring + w, ring + w, c0 + 1 < h ? ring + 2 * w : ring + w,
-                               rc, ak, pr);
-            }
-        }
-        __syncthreads();
+    // deferred first row: rows c0-1 (the previous strip's published row), c0
+    // and c0+1 go back into ring slots 0, 1, 2
+    __shared__ int s_ok;
+    compute_rowco<KH>(d, c0, rowco[c0 & 1]);
+    if (c0 > 0 && threadIdx.x == 0) {
+        const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
+        if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
+        s_ok = ok;
     }
-    gstep += (uint64_t)nsteps;
+    __syncthreads();
+    const float2 *prev = pub - (sidx > 0 ? w : 0);
+    const bool ok = c0 > 0 && s_ok;
+    const bool next = c0 + 1 < h;
+    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+        if (c0 > 0) ring[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
+        ring[w + j] = __ldcg(head + j);
+        if (next) ring[2 * w + j] = __ldcg(head + w + j);
+    }
+    __syncthreads();
+    const float2 *R[3] = {c0 > 0 ? ring : ring + w, ring + w, next ? ring + 2 * w : ring + w};
+    phase2<KH, KW>(d, c0, R, rowco[c0 & 1], ak);
+    __syncthreads();
 }
 
 __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s) {
@@ -748,35 +541,27 @@ __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s)
     return lo;
 }
 
-template <int KH, int KW>
-__global__ void __launch_bounds__(kThreads, 2)
+template <int KH, int KW, int CELLS, int MINB>
+__global__ void __launch_bounds__(kFusedThreads, MINB)
     fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
-                      float *heads, int64_t head_stride, int32_t max_w, int32_t rstate_stride, int64_t wait_iters) {
-    using G = Geo<KH, KW>;
-    extern __shared__ __align__(128) unsigned char dyn[];
-    __shared__ SharedCtl ctl;
-    float *stages = reinterpret_cast<float *>(dyn);
-    float2 *ring = reinterpret_cast<float2 *>(stages + (size_t)kStages * G::STAGE_FLOATS);
-    char *rstate = reinterpret_cast<char *>(ring + 3 * (size_t)max_w);
+                      float *heads, int64_t head_stride, int64_t wait_iters) {
+    extern __shared__ float2 ring[];
+    __shared__ RowCo rowco[2][KH];
+    __shared__ int64_t s_strip;
+    __shared__ unsigned int s_epoch;
+    if (threadIdx.x == 0) s_epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
     float2 *head = reinterpret_cast<float2 *>(heads + (int64_t)blockIdx.x * head_stride);
-    if (threadIdx.x == 0) {
-        ctl.epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
-        for (int i = 0; i < kStages; i++) mbar_init(&ctl.bar[i], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    uint64_t gstep = 0;
     const int64_t total = b.strip_start[b.n];
     for (;;) {
-        if (threadIdx.x == 0) ctl.strip = (int64_t)atomicAdd(&hdr->next_item, 1u);
+        if (threadIdx.x == 0) s_strip = (int64_t)atomicAdd(&hdr->next_item, 1u);
         __syncthreads();
-        const int64_t s = ctl.strip;
-        const unsigned int epoch = ctl.epoch;
+        const int64_t s = s_strip;
+        const unsigned int epoch = s_epoch;
         __syncthreads();
         if (s >= total) break;
         const int t = find_strip_tensor(b, s);
-        process_strip<KH, KW>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, stages, ring, rstate, rstate_stride, head,
-                              ctl, gstep, hdr, flags, halo, wait_iters);
+        process_strip<KH, KW, CELLS>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags, halo,
+                              wait_iters);
     }
     if (threadIdx.x == 0) {
         __threadfence();
@@ -785,7 +570,7 @@ __global__ void __launch_bounds__(kThreads, 2)
             // last CTA out: reset the scheduler for the next launch, advance the epoch
             hdr->next_item = 0;
             hdr->done_ctas = 0;
-            hdr->epoch = ctl.epoch;
+            hdr->epoch = s_epoch;
             __threadfence();
         }
     }
@@ -828,18 +613,12 @@ bool fused_takes(const smo_tensor &t) {
     if (t.rows % t.comp_rows != 0 || t.cols % t.comp_cols != 0) return false;
     const int64_t kh = t.rows / t.comp_rows, kw = t.cols / t.comp_cols;
     if (!supported_window(kh) || !supported_window(kw)) return false;
-    if (t.cols <= 128) return false;                  // torch's small-output interpolation order
-    if (t.comp_cols % 16 != 0) return false;          // 16-byte TMA / cp.async granules of every row
+    if (t.cols <= 128) return false;  // torch's small-output interpolation order
     if (t.comp_cols > kMaxFusedCols) return false;
     if (t.comp_rows * t.comp_cols >= ((int64_t)1 << 31)) return false;  // 32-bit cell indices
     if (t.kind == SMO_KIND_POOLED8 && t.q_block > t.comp_cols) return false;
-    if ((uintptr_t)t.param % 16 || (uintptr_t)t.grad % 16) return false;
-    if (t.kind == SMO_KIND_POOLED8) {
-        if ((uintptr_t)t.m_q_in % 16 || (uintptr_t)t.v_q_in % 16) return false;
-        if ((uintptr_t)t.m_s_in % 4 || (uintptr_t)t.v_s_in % 4) return false;
-    } else {
-        if ((uintptr_t)t.m_in % 16 || (uintptr_t)t.v_in % 16) return false;
-    }
+    const size_t a = kw % 4 == 0 ? 16 : 8;
+    if ((uintptr_t)t.param % a || (uintptr_t)t.grad % a) return false;
     if (t.interp_band < 0) return false;
     // the look-ahead reads the next strip's OLD state while that strip writes
     // the new one: in-place state would race, so it needs separate buffers
@@ -862,11 +641,15 @@ static int window_key(const smo_tensor &t) {
     return (int)((t.rows / t.comp_rows) * 16 + (t.cols / t.comp_cols));
 }
 
-// bytes of one row-state buffer (see RowState)
-static int64_t row_state_bytes(const smo_tensor &t) {
-    const int64_t w = t.comp_cols;
-    if (t.kind == SMO_KIND_POOLED8) return 2 * w + 8 * (w / t.q_block + 2);
-    return 8 * w;
+// Tuning override for measurements: SMO_B200_FUSED_VARIANT=1 selects two
+// cells per iteration at 2 CTAs/SM (128 registers) for every window.
+static int fused_variant() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("SMO_B200_FUSED_VARIANT");
+        v = e ? atoi(e) : 0;
+    }
+    return v;
 }
 
 static int device_sm_count() {
@@ -898,17 +681,16 @@ size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
 }
 
 template <int KH, int KW>
-static int launch_fused_group(FusedBatch &b, int64_t max_w, int64_t max_rs, size_t halo_floats, char *ws,
-                              cudaStream_t stream) {
-    using G = Geo<KH, KW>;
-    const int rstride = (int)((max_rs + 15) / 16 * 16);
-    const size_t smem = (size_t)kStages * G::STAGE_FLOATS * sizeof(float) + 3 * (size_t)max_w * sizeof(float2) +
-                        2 * (size_t)rstride;
-    auto kern = fused_step_kernel<KH, KW>;
+static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
+    const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
+    // 16-element windows: one cell per thread-iteration at 3 CTAs/SM (80
+    // registers); smaller windows: two cells per iteration
+    auto kern = (KH * KW >= 16) ? fused_step_kernel<KH, KW, 1, 3> : fused_step_kernel<KH, KW, 2, 3>;
+    if (fused_variant() == 1) kern = fused_step_kernel<KH, KW, 2, 2>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedThreads, smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
     const int64_t strips = b.strip_start[b.n];
@@ -921,19 +703,17 @@ static int launch_fused_group(FusedBatch &b, int64_t max_w, int64_t max_rs, size
     float *halo = (float *)body;
     body += align_up(halo_floats * sizeof(float));
     float *heads = (float *)body;
-    kern<<<(unsigned)grid, kThreads, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, (int32_t)max_w, rstride,
-                                                     kDefaultWaitIters);
+    kern<<<(unsigned)grid, kFusedThreads, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;
     return SMO_OK;
 }
 
-static int dispatch(int key, FusedBatch &b, int64_t max_w, int64_t max_rs, size_t halo_floats, char *ws,
-                    cudaStream_t stream) {
+static int dispatch(int key, FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
     switch (key) {
 #define SMO_FUSED_CASE(KH, KW) \
-    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, max_rs, halo_floats, ws, stream);
+    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, halo_floats, ws, stream);
         SMO_FUSED_CASE(2, 2) SMO_FUSED_CASE(2, 4) SMO_FUSED_CASE(2, 8)
         SMO_FUSED_CASE(4, 2) SMO_FUSED_CASE(4, 4) SMO_FUSED_CASE(4, 8)
         SMO_FUSED_CASE(8, 2) SMO_FUSED_CASE(8, 4) SMO_FUSED_CASE(8, 8)
@@ -954,6 +734,7 @@ static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off) {
     f.B = t.kind == SMO_KIND_POOLED8 ? (int32_t)t.q_block : 1;
     f.L = (int32_t)strip_rows(t);
     f.div_B = make_fast_div((uint32_t)f.B);
+    f.div_w = make_fast_div((uint32_t)f.w);
     f.halo_off = halo_off;
     f.kind = t.kind;
     f.hp = t.hp;
@@ -970,7 +751,7 @@ int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaSt
         const int key = window_key(t[i]);
         batch.n = 0;
         batch.strip_start[0] = 0;
-        int64_t halo_off = 0, max_w = 0, max_rs = 0;
+        int64_t halo_off = 0, max_w = 0;
         for (int32_t k = i; k < n && batch.n < kMaxFused; k++) {
             if (done[k] || window_key(t[k]) != key) continue;
             FusedDesc &f = batch.d[batch.n];
@@ -978,15 +759,13 @@ int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaSt
             const int64_t s = num_strips(t[k]);
             halo_off += s * 2 * t[k].comp_cols;
             max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
-            const int64_t rs = row_state_bytes(t[k]);
-            max_rs = max_rs > rs ? max_rs : rs;
             batch.strip_start[batch.n + 1] = batch.strip_start[batch.n] + s;
             batch.n++;
             done[k] = 1;
         }
         // tensors of the same window left over (batch full) start a new batch when
         // the scan reaches them
-        const int st = dispatch(key, batch, max_w, max_rs, (size_t)halo_off, ws, stream);
+        const int st = dispatch(key, batch, max_w, (size_t)halo_off, ws, stream);
         if (st != SMO_OK) return st;
     }
     return SMO_OK;
