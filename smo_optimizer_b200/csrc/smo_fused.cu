@@ -41,7 +41,6 @@
 
 namespace smo {
 
-constexpr int kFusedThreads = 256;
 constexpr int kMaxFusedCtasPerSm = 4;
 constexpr int kMaxFused = 104;
 constexpr int64_t kStripRows = 16;          // target compact rows per strip
@@ -284,7 +283,7 @@ __device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, floa
 // Phase 1 of compact row c: post-EMA (m, v) into `row` (shared memory).
 // `own` rows also write the fp32 state (POOLED32); look-ahead rows only read.
 // CELLS cells per thread per iteration keep CELLS*KH*KW*2 loads in flight.
-template <int KH, int KW, int CELLS, bool WD>
+template <int KH, int KW, int CELLS, int NT, bool WD>
 __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row, bool own) {
     const int w = d.w;
     const int64_t W = d.W;
@@ -292,11 +291,11 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
     const float *pb = d.p + (int64_t)c * KH * W;
     const uint32_t cell0 = (uint32_t)c * (uint32_t)w;
     const float wd = d.hp.weight_decay;
-    for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * kFusedThreads) {
+    for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * NT) {
         float gv[CELLS][KH][KW], pv[CELLS][KH][KW];
 #pragma unroll
         for (int u = 0; u < CELLS; u++) {
-            const int j = j0 + u * kFusedThreads;
+            const int j = j0 + u * NT;
             if (u == 0 || j < w) {
 #pragma unroll
                 for (int i = 0; i < KH; i++) load_grad_row<KW>(gb + i * W + (int64_t)j * KW, gv[u][i]);
@@ -308,16 +307,16 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
         }
 #pragma unroll
         for (int u = 0; u < CELLS; u++) {
-            const int j = j0 + u * kFusedThreads;
+            const int j = j0 + u * NT;
             if (u == 0 || j < w) ema_cell(d, cell0 + j, pool_cell<KH, KW, WD>(gv[u], pv[u], wd), row, j, own);
         }
     }
 }
 
-template <int KH, int KW, int CELLS>
+template <int KH, int KW, int CELLS, int NT>
 __device__ __forceinline__ void phase1(const FusedDesc &d, int c, float2 *row, bool own) {
-    if (d.hp.wd_on) phase1_wd<KH, KW, CELLS, true>(d, c, row, own);
-    else phase1_wd<KH, KW, CELLS, false>(d, c, row, own);
+    if (d.hp.wd_on) phase1_wd<KH, KW, CELLS, NT, true>(d, c, row, own);
+    else phase1_wd<KH, KW, CELLS, NT, false>(d, c, row, own);
 }
 
 // Requantise the int8 blocks that compact row c completes.  A block spans at
@@ -350,13 +349,14 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
     }
 }
 
+template <int NT>
 __device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const float2 *Rc, const float2 *Rp) {
     const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
     const uint32_t b_lo = fast_div((uint32_t)c * w, d.div_B);
     uint32_t b_hi = fast_div(((uint32_t)c + 1u) * w, d.div_B);
     if (c == d.h - 1 && C % B != 0) b_hi = C / B + 1;  // the zero-padded last block
     const bool aligned = (w % B) == 0;                  // blocks never leave the row
-    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += kFusedThreads / 32)
+    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += NT / 32)
         requant_block(d, b, c, Rc, Rp, aligned);
 }
 
@@ -390,12 +390,12 @@ __device__ __forceinline__ float col_l1(int t) {
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
 // c-1 (R[0]), c (R[1]), c+1 (R[2]) in shared memory (an absent neighbour row
 // is passed as row c and never weighted).  Row weights come from `rowco`.
-template <int KH, int KW>
+template <int KH, int KW, int NT>
 __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
                                        const AdamK &ak) {
     const int w = d.w;
     const int64_t W = d.W;
-    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+    for (int j = threadIdx.x; j < w; j += NT) {
         float *pbase = d.p + (int64_t)c * KH * W + (int64_t)j * KW;
         float pv[KH][KW];
 #pragma unroll
@@ -446,7 +446,7 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
 
 // One strip: phase-1 rows r = c0 .. c1 (c1 = look-ahead row, when it exists),
 // each followed by phase 2 of row r-1; then the strip's first row.
-template <int KH, int KW, int CELLS>
+template <int KH, int KW, int CELLS, int NT>
 __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float2 *ring,
                               float2 *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
                               int64_t wait_iters) {
@@ -467,17 +467,17 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     auto save_head = [&](int c, int slot) {
         const float2 *src = RR(c);
         float2 *dst = head + slot * w;
-        for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(dst + j, src[j]);
+        for (int j = threadIdx.x; j < w; j += NT) __stcg(dst + j, src[j]);
     };
 
     for (int r = c0; r <= last; r++) {
         const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
         if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
         if (r < last) prefetch_row_l2<KH>(d, r + 1);
-        phase1<KH, KW, CELLS>(d, r, RR(r), r < c1);
+        phase1<KH, KW, CELLS, NT>(d, r, RR(r), r < c1);
         __syncthreads();
         if (r < c1) {
-            if (q8) requant_row(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
+            if (q8) requant_row<NT>(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
             if (r == c0) save_head(r, 0);
             if (r == c0 + 1) save_head(r, 1);
         } else {
@@ -486,7 +486,7 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
             // (after the look-ahead read of that strip's parameters and state)
             if (r == c0 + 1) save_head(r, 1);
             const float2 *src = RR(c1 - 1);
-            for (int j = threadIdx.x; j < w; j += kFusedThreads) __stcg(pub + j, src[j]);
+            for (int j = threadIdx.x; j < w; j += NT) __stcg(pub + j, src[j]);
             __syncthreads();
             if (threadIdx.x == 0) {
                 __threadfence();
@@ -495,7 +495,7 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         }
         if (do2) {
             const float2 *R[3] = {RR(r - 2), RR(r - 1), RR(r)};
-            phase2<KH, KW>(d, r - 1, R, rowco[(r - 1) & 1], ak);
+            phase2<KH, KW, NT>(d, r - 1, R, rowco[(r - 1) & 1], ak);
         }
         __syncthreads();
     }
@@ -504,7 +504,7 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         compute_rowco<KH>(d, c1 - 1, rowco[(c1 - 1) & 1]);
         __syncthreads();
         const float2 *R[3] = {RR(c1 - 2), RR(c1 - 1), RR(c1 - 1)};
-        phase2<KH, KW>(d, c1 - 1, R, rowco[(c1 - 1) & 1], ak);
+        phase2<KH, KW, NT>(d, c1 - 1, R, rowco[(c1 - 1) & 1], ak);
         __syncthreads();
     }
 
@@ -521,14 +521,14 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     const float2 *prev = pub - (sidx > 0 ? w : 0);
     const bool ok = c0 > 0 && s_ok;
     const bool next = c0 + 1 < h;
-    for (int j = threadIdx.x; j < w; j += kFusedThreads) {
+    for (int j = threadIdx.x; j < w; j += NT) {
         if (c0 > 0) ring[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
         ring[w + j] = __ldcg(head + j);
         if (next) ring[2 * w + j] = __ldcg(head + w + j);
     }
     __syncthreads();
     const float2 *R[3] = {c0 > 0 ? ring : ring + w, ring + w, next ? ring + 2 * w : ring + w};
-    phase2<KH, KW>(d, c0, R, rowco[c0 & 1], ak);
+    phase2<KH, KW, NT>(d, c0, R, rowco[c0 & 1], ak);
     __syncthreads();
 }
 
@@ -541,8 +541,8 @@ __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s)
     return lo;
 }
 
-template <int KH, int KW, int CELLS, int MINB>
-__global__ void __launch_bounds__(kFusedThreads, MINB)
+template <int KH, int KW, int CELLS, int NT, int MINB>
+__global__ void __launch_bounds__(NT, MINB)
     fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
                       float *heads, int64_t head_stride, int64_t wait_iters) {
     extern __shared__ float2 ring[];
@@ -560,7 +560,7 @@ __global__ void __launch_bounds__(kFusedThreads, MINB)
         __syncthreads();
         if (s >= total) break;
         const int t = find_strip_tensor(b, s);
-        process_strip<KH, KW, CELLS>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags, halo,
+        process_strip<KH, KW, CELLS, NT>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags, halo,
                               wait_iters);
     }
     if (threadIdx.x == 0) {
@@ -641,15 +641,24 @@ static int window_key(const smo_tensor &t) {
     return (int)((t.rows / t.comp_rows) * 16 + (t.cols / t.comp_cols));
 }
 
-// Tuning override for measurements: SMO_B200_FUSED_VARIANT=1 selects two
-// cells per iteration at 2 CTAs/SM (128 registers) for every window.
-static int fused_variant() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("SMO_B200_FUSED_VARIANT");
-        v = e ? atoi(e) : 0;
+// CTA width of a launch: 256 or 384 threads, whichever leaves fewer idle
+// thread-columns over the batch's compact rows (a compact row of w cells takes
+// ceil(w / NT) passes of NT threads); ties go to 384.  SMO_B200_FUSED_THREADS
+// (256 or 384) forces one width, for measurements.
+static int pick_threads(const FusedBatch &b) {
+    static int forced = -1;
+    if (forced < 0) {
+        const char *e = getenv("SMO_B200_FUSED_THREADS");
+        forced = e ? atoi(e) : 0;
     }
-    return v;
+    if (forced == 256 || forced == 384) return forced;
+    int64_t idle256 = 0, idle384 = 0;
+    for (int i = 0; i < b.n; i++) {
+        const int64_t w = b.d[i].w, rows = b.d[i].h;
+        idle256 += rows * ((w + 255) / 256 * 256 - w);
+        idle384 += rows * ((w + 383) / 384 * 384 - w);
+    }
+    return idle384 <= idle256 ? 384 : 256;
 }
 
 static int device_sm_count() {
@@ -680,17 +689,26 @@ size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
            ctas * 4 * (size_t)max_w * sizeof(float);
 }
 
+// The kernel instance of a window shape and CTA width: 16-element windows take
+// one cell per thread-iteration, smaller windows two; 384-thread CTAs run two
+// per SM (80 registers), 256-thread CTAs four (one cell, 64 registers) or
+// three (two cells, 80 registers).
+template <int KH, int KW>
+static auto fused_kernel_for(int nt) {
+    constexpr int kCells = KH * KW >= 16 ? 1 : 2;
+    constexpr int kMinBlocks256 = kCells == 1 ? 4 : 3;
+    return nt == 384 ? fused_step_kernel<KH, KW, kCells, 384, 2> : fused_step_kernel<KH, KW, kCells, 256, kMinBlocks256>;
+}
+
 template <int KH, int KW>
 static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
     const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
-    // 16-element windows: one cell per thread-iteration at 3 CTAs/SM (80
-    // registers); smaller windows: two cells per iteration
-    auto kern = (KH * KW >= 16) ? fused_step_kernel<KH, KW, 1, 3> : fused_step_kernel<KH, KW, 2, 3>;
-    if (fused_variant() == 1) kern = fused_step_kernel<KH, KW, 2, 2>;
+    const int nt = pick_threads(b);
+    auto kern = fused_kernel_for<KH, KW>(nt);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kFusedThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nt, smem);
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
     const int64_t strips = b.strip_start[b.n];
@@ -703,7 +721,7 @@ static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, 
     float *halo = (float *)body;
     body += align_up(halo_floats * sizeof(float));
     float *heads = (float *)body;
-    kern<<<(unsigned)grid, kFusedThreads, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
+    kern<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
     e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;
