@@ -8,8 +8,8 @@ One "step" is one optimizer step over the whole parameter set of the workload
 synthetic grads ~N(0, 1e-3)).  With N > 1 (launched by torch.distributed.run)
 the tensors are sharded ZeRO-1 style: each rank steps the tensors it owns, and
 ``value`` is all ranks' params / the slowest rank's device time.  The NCCL
-broadcast of updated params that completes a ZeRO-1 step is timed separately
-(``zero1``).  Rank 0 prints one JSON line.
+all-gather of the flat parameter buffer that completes a ZeRO-1 step is timed
+separately (``zero1``).  Rank 0 prints one JSON line.
 
 ``--impl reference`` times the CPU restatement of the reference step (the
 oracle, all host threads) on the same workload, one tensor per step in
@@ -258,6 +258,11 @@ def main():
     owner = zero.lpt_partition(costs, world)
     owned = [o == rank for o in owner]
     params, grads = build_workload(wl, args.seed, device, owned)
+    flat = None
+    if world > 1:
+        # ZeRO-1 layout: parameters rebound into one rank-contiguous buffer so the
+        # exchange after the step is a single in-place all-gather
+        flat = zero.FlatParams(params, owner, world, rank).bind()
     mine = [p for p, o in zip(params, owned) if o]
     if wl.protect_output:
         named = [(n, p) for (n, _), p, o in zip(wl.tensors, params, owned) if o]
@@ -324,28 +329,31 @@ def main():
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
             "algorithmic_bytes_per_launch": my_bytes, "traffic": load_traffic(wl.name, "step")}
 
-    # ---- ZeRO-1 completion: broadcast of updated params from their owners
+    # ---- ZeRO-1 completion: one in-place all-gather of the flat parameter buffer
     zero1 = None
     if world > 1:
-        z = zero.Zero1.__new__(zero.Zero1)
-        z.group, z.world, z.rank, z.params, z.owner = None, world, rank, params, owner
         for _ in range(3):
-            z.broadcast_params()
+            flat.all_gather()
         torch.cuda.synchronize()
         barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         nb = 10
         a.record(stream)
         for _ in range(nb):
-            opt.step()
-            z.broadcast_params()
+            flat.all_gather()
         b.record(stream)
+        for _ in range(nb):
+            opt.step()
+            flat.all_gather()
+        c.record(stream)
         torch.cuda.synchronize()
-        t = torch.tensor([a.elapsed_time(b) / nb], device=device)
+        t = torch.tensor([a.elapsed_time(b) / nb, b.elapsed_time(c) / nb], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        zms = float(t[0])
-        zero1 = {"step_plus_broadcast_ms": zms, "params_per_s": total_params / (zms * 1e-3),
-                 "broadcast_bytes_per_rank": 4 * (total_params - my_params)}
+        ag_ms, zms = float(t[0]), float(t[1])
+        zero1 = {"step_plus_allgather_ms": zms, "allgather_ms": ag_ms,
+                 "params_per_s": total_params / (zms * 1e-3),
+                 "allgather_bytes_per_rank": flat.bytes_per_rank,
+                 "allgather_busbw_gbs": flat.bytes_per_rank / (ag_ms * 1e-3) / 1e9}
 
     # ---- e2e through the public API with host buffers (pinned): H2D grads, step, D2H params
     e2e = None

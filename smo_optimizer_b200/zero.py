@@ -3,10 +3,18 @@
 Each rank owns a subset of the parameter tensors (chosen by a greedy
 longest-processing-time partition on the step's algorithmic bytes), keeps the
 optimizer state for those tensors only, steps them locally, and then the
-updated parameters are broadcast from their owners so every replica holds the
-same weights.  The reference has no distributed code; this is the build's own
-multi-GPU layer.  Tensors are independent, so the step itself needs no
-exchange: the only collective is the parameter broadcast/all-gather after it.
+updated parameters are exchanged so every replica holds the same weights.
+The reference has no distributed code; this is the build's own multi-GPU
+layer.  Tensors are independent, so the step itself needs no exchange: the
+only collective is the parameter exchange after it.
+
+Two exchanges:
+  * flat (default when every parameter has the same device and dtype): the
+    parameters are rebound to views of one rank-contiguous buffer (rank r's
+    tensors in slot r, slots padded to the largest rank's size), so one
+    in-place all-gather completes the step, with every link busy in both
+    directions;
+  * per tensor: an async broadcast of each tensor from its owner.
 """
 
 from __future__ import annotations
@@ -61,16 +69,69 @@ def rank_loads(costs, owner, world: int):
     return loads
 
 
+class FlatParams:
+    """Rank-contiguous flat parameter buffer for the one-collective exchange.
+
+    Rank r's owned tensors sit one after another in slot r of ``buffer``
+    (``shard`` elements per slot, the largest rank's total rounded up); each
+    tensor starts on a 64-element (256-byte) boundary, which keeps the fused
+    kernel's 16-byte vector loads aligned.  ``bind()`` copies every parameter
+    into its place and rebinds ``p.data`` to that view.
+    """
+
+    ALIGN = 64
+
+    def __init__(self, params, owner, world: int, rank: int):
+        params = list(params)
+        if not params:
+            raise ValueError("no parameters")
+        dev, dtype = params[0].device, params[0].dtype
+        if any(p.device != dev or p.dtype != dtype for p in params):
+            raise ValueError("flat exchange needs one device and one dtype for every parameter")
+        self.params, self.owner, self.world, self.rank = params, list(owner), world, rank
+        fill = [0] * world
+        self.offsets = []
+        for p, r in zip(params, self.owner):
+            self.offsets.append(fill[r])
+            fill[r] += (p.numel() + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+        self.shard = max(max(fill), self.ALIGN)
+        self.buffer = torch.zeros(world * self.shard, dtype=dtype, device=dev)
+
+    def bind(self):
+        with torch.no_grad():
+            for p, r, off in zip(self.params, self.owner, self.offsets):
+                view = self.buffer.narrow(0, r * self.shard + off, p.numel()).view(p.shape)
+                view.copy_(p.data)
+                p.data = view
+        return self
+
+    def local_slot(self):
+        return self.buffer.narrow(0, self.rank * self.shard, self.shard)
+
+    def all_gather(self, group=None, async_op: bool = False):
+        """Every rank's slot to every rank, in place (input = this rank's slot)."""
+        return dist.all_gather_into_tensor(self.buffer, self.local_slot(), group=group, async_op=async_op)
+
+    @property
+    def bytes_per_rank(self) -> int:
+        return (self.world - 1) * self.shard * self.buffer.element_size()
+
+
 class Zero1:
     """ZeRO-1 wrapper around ``SMO`` / ``SMO8bit``.
 
     ``Zero1(params, SMO8bit, lr=..., ...)`` builds the inner optimizer over the
-    tensors this rank owns.  ``step()`` steps them and then broadcasts every
-    tensor from its owner (NCCL over NVLink for CUDA tensors), so all ranks end
-    the step with identical parameters.  ``state_dict()`` is this rank's shard.
+    tensors this rank owns.  ``step()`` steps them and then exchanges the
+    updated tensors (NCCL over NVLink for CUDA tensors), so all ranks end the
+    step with identical parameters.  ``state_dict()`` is this rank's shard.
+
+    ``flat=True`` (default) rebinds the parameters to views of one flat
+    buffer (see ``FlatParams``) and exchanges with a single all-gather; it
+    falls back to per-tensor broadcasts when the parameters differ in device
+    or dtype.  ``flat=False`` always broadcasts per tensor.
     """
 
-    def __init__(self, params, optimizer_cls, process_group=None, **kwargs):
+    def __init__(self, params, optimizer_cls, process_group=None, flat: bool = True, **kwargs):
         self.group = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
@@ -80,6 +141,9 @@ class Zero1:
                             kwargs.get("block_size", 64), kwargs.get("compress_conv", False)) for p in self.params]
         self.owner = lpt_partition(costs, self.world)
         self.costs = costs
+        self.flat = None
+        if flat and self.world > 1 and len({(p.device, p.dtype) for p in self.params}) == 1:
+            self.flat = FlatParams(self.params, self.owner, self.world, self.rank).bind()
         self.owned = [p for p, r in zip(self.params, self.owner) if r == self.rank]
         self.optimizer = optimizer_cls(self.owned, **kwargs) if self.owned else None
 
@@ -102,13 +166,22 @@ class Zero1:
         for w in works:
             w.wait()
 
+    def exchange_params(self):
+        """Bring every rank's updated tensors to all ranks."""
+        if self.world == 1:
+            return
+        if self.flat is not None:
+            self.flat.all_gather(self.group)
+        else:
+            self.broadcast_params()
+
     def step(self, closure=None):
         loss = None
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
         self.local_step()
-        self.broadcast_params()
+        self.exchange_params()
         return loss
 
     def zero_grad(self, set_to_none: bool = True):

@@ -1,5 +1,6 @@
 """ZeRO-1 host logic on CPU ranks (gloo, world_size 2): the partition, the
-owner-to-all parameter broadcast, and a rank failing before the broadcast.
+flat all-gather and the per-tensor broadcast exchanges, and a rank failing
+before the exchange.
 
 The CUDA step cannot run on the CPU, so the ranks use a stand-in optimizer
 (plain SGD on their owned tensors); what is under test is the sharding and the
@@ -51,7 +52,14 @@ def _worker(rank, world, port, mode, out):
         grads = _params(1)
         for p, g in zip(params, grads):
             p.grad = g.clone()
-        z = zero.Zero1(params, StandIn, lr=0.5)
+        z = zero.Zero1(params, StandIn, lr=0.5, flat=(mode != "bcast"))
+        if mode != "bcast":
+            # every parameter is a 256-byte aligned view of the one flat buffer
+            base = z.flat.buffer.data_ptr()
+            assert all(p.data_ptr() % 256 == base % 256 and
+                       base <= p.data_ptr() < base + z.flat.buffer.numel() * 4 for p in params)
+        else:
+            assert z.flat is None
         if mode == "fail" and rank == 1:
             raise SystemExit(3)  # this rank dies before the broadcast
         t0 = time.time()
@@ -92,6 +100,24 @@ def test_lpt_partition_is_deterministic_and_balanced():
     assert zero.lpt_partition(costs, 1) == [0] * len(costs)
 
 
+def test_flat_layout_is_rank_contiguous_and_padded():
+    params = [torch.nn.Parameter(t) for t in _params(0)]
+    owner = [0, 1, 1, 0, 1, 0, 0]
+    f = zero.FlatParams(params, owner, 2, 1)
+    ref = [t.clone() for t in _params(0)]
+    f.bind()
+    sizes = [0, 0]
+    for p, r, off, e in zip(params, owner, f.offsets, ref):
+        assert off == sizes[r] and off % 64 == 0
+        sizes[r] += (p.numel() + 63) // 64 * 64
+        assert torch.equal(p.data, e)
+        assert p.data.data_ptr() == f.buffer.data_ptr() + 4 * (r * f.shard + off)
+    assert f.shard == max(sizes) and f.local_slot().numel() == f.shard
+    assert f.bytes_per_rank == 4 * f.shard
+    with pytest.raises(ValueError):
+        zero.FlatParams([torch.zeros(4), torch.zeros(4, dtype=torch.float64)], [0, 1], 2, 0)
+
+
 def test_step_bytes_formula():
     # pooled int8, 1024x1024 at k=0.25: 12 B/param + 4 B/cell + 16 B/block
     assert zero.step_bytes((1024, 1024), "SMO8bit") == 12 * 1024 * 1024 + 4 * 65536 + 16 * 1024
@@ -99,8 +125,9 @@ def test_step_bytes_formula():
     assert zero.step_bytes((1024, 1024), "SMO", k_ratio=0.5) == 12 * 1024 * 1024 + 16 * 512 * 512
 
 
-def test_zero1_broadcast_makes_replicas_identical():
-    out, codes = _run("ok")
+@pytest.mark.parametrize("mode", ["ok", "bcast"])
+def test_zero1_exchange_makes_replicas_identical(mode):
+    out, codes = _run(mode)
     assert codes == [0, 0]
     (s0, p0, own0), (s1, p1, own1) = out[0], out[1]
     assert s0 == s1 == "ok" and own0 == own1 and set(own0) == {0, 1}
