@@ -176,6 +176,18 @@ SMO_API int smo_synth_normal(float *out, int64_t n, uint64_t base, float scale, 
 SMO_API int smo_selftest_wait_timeout(void *workspace, size_t workspace_bytes, int64_t max_iters, int32_t *status_out,
                               void *stream);
 
+/* Self-test of the fused step's FMA-only square root, reciprocal and division
+ * (approximation + Markstein corrections) against the IEEE operations on this
+ * device, over the input ranges where the step relies on them being exact:
+ * counts_out[0] = finite v >= 2^-102 (all of them) whose square root differs,
+ * counts_out[1] = normal d in [2^-126, 2^126] (all of them) whose reciprocal
+ * differs, counts_out[2] = differing quotients among n_pairs pseudo-random
+ * in-range pairs, counts_out[3] = quotients checked.  Uses only the workspace
+ * header (>= 256 bytes, 256-byte aligned) and waits for the stream.  No
+ * counterpart in the reference. */
+SMO_API int smo_selftest_fastmath(void *workspace, size_t workspace_bytes, uint64_t n_pairs, uint64_t *counts_out,
+                                  void *stream);
+
 /* Number of kernels this library has launched in this process (all devices,
  * all entry points), for launch accounting in benchmarks. */
 SMO_API uint64_t smo_launch_count(void);

@@ -75,6 +75,7 @@ def load():
         "smo_upsample2d": (ctypes.c_int, [P, i64, i64, i64, i64, i64, P, P]),
         "smo_synth_normal": (ctypes.c_int, [P, i64, ctypes.c_uint64, ctypes.c_float, i64, P]),
         "smo_selftest_wait_timeout": (ctypes.c_int, [P, sz, i64, ctypes.POINTER(ctypes.c_int32), P]),
+        "smo_selftest_fastmath": (ctypes.c_int, [P, sz, ctypes.c_uint64, ctypes.POINTER(ctypes.c_uint64), P]),
         "smo_status_string": (ctypes.c_char_p, [ctypes.c_int]),
         "smo_last_cuda_error": (ctypes.c_int, []),
         "smo_abi_version": (ctypes.c_int, []),

@@ -279,6 +279,64 @@ __global__ void selftest_wait_kernel(const unsigned int *flag, int64_t max_iters
     if (threadIdx.x == 0 && blockIdx.x == 0) *status = st;
 }
 
+// Check of the FMA-only arithmetic of the fused step (smo_common.cuh) against
+// the IEEE operations, on this device:
+//   counts[0]: finite v >= 2^-102 (every one) where sqrt2_markstein differs
+//              from __fsqrt_rn;
+//   counts[1]: normal d in [2^-126, 2^126] (every one) where rcp2_newton
+//              differs from __frcp_rn;
+//   counts[2]: pseudo-random pairs (a of either sign, exponent -60..20; d in
+//              [2^-27, 2^21)) with |q0| in [2^-76, 2^100] where div2_markstein
+//              differs from __fdiv_rn;  counts[3]: pairs checked.
+__device__ __forceinline__ uint64_t selftest_mix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void selftest_fastmath_kernel(uint64_t n_pairs, unsigned long long *counts) {
+    unsigned long long bad_sqrt = 0, bad_rcp = 0, bad_div = 0, checked = 0;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t first = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+    // square roots: bit patterns 2^-102 .. max finite, two per iteration
+    const uint64_t s_lo = 0x0c800000ull, s_n = (0x7f7fffffull - s_lo + 2) / 2;
+    for (uint64_t i = first; i < s_n; i += stride) {
+        const uint32_t b0 = (uint32_t)(s_lo + 2 * i), b1 = b0 + 1 <= 0x7f7fffffu ? b0 + 1 : b0;
+        const float2 v = make_float2(__uint_as_float(b0), __uint_as_float(b1));
+        const float2 r = sqrt2_markstein(v);
+        bad_sqrt += (__float_as_uint(r.x) != __float_as_uint(__fsqrt_rn(v.x)));
+        bad_sqrt += (__float_as_uint(r.y) != __float_as_uint(__fsqrt_rn(v.y)));
+    }
+    // reciprocals: 2^-126 .. 2^126
+    const uint64_t r_lo = 0x00800000ull, r_n = (0x7e800000ull - r_lo + 2) / 2;
+    for (uint64_t i = first; i < r_n; i += stride) {
+        const uint32_t b0 = (uint32_t)(r_lo + 2 * i), b1 = b0 + 1 <= 0x7e800000u ? b0 + 1 : b0;
+        const float2 d = make_float2(__uint_as_float(b0), __uint_as_float(b1));
+        const float2 r = rcp2_newton(d);
+        bad_rcp += (__float_as_uint(r.x) != __float_as_uint(__frcp_rn(d.x)));
+        bad_rcp += (__float_as_uint(r.y) != __float_as_uint(__frcp_rn(d.y)));
+    }
+    for (uint64_t i = first; i < n_pairs; i += stride) {
+        const uint64_t h = selftest_mix(i);
+        const uint32_t ea = 127 - 60 + (uint32_t)((h >> 32) % 81), ed = 127 - 27 + (uint32_t)((h >> 48) % 48);
+        const float a = __uint_as_float(((uint32_t)(h >> 31) & 0x80000000u) | (ea << 23) | ((uint32_t)h & 0x7fffffu));
+        const float d = __uint_as_float((ed << 23) | ((uint32_t)(h >> 8) & 0x7fffffu));
+        const float2 a2 = make_float2(a, -a), d2 = make_float2(d, d);
+        float2 q0;
+        const float2 q = div2_markstein(a2, d2, rcp2_newton(d2), q0);
+        if (fabsf(q0.x) >= 0x1p-76f && fabsf(q0.x) <= 0x1p100f) {
+            checked += 2;
+            bad_div += (__float_as_uint(q.x) != __float_as_uint(__fdiv_rn(a, d)));
+            bad_div += (__float_as_uint(q.y) != __float_as_uint(__fdiv_rn(-a, d)));
+        }
+    }
+    if (bad_sqrt) atomicAdd(&counts[0], bad_sqrt);
+    if (bad_rcp) atomicAdd(&counts[1], bad_rcp);
+    if (bad_div) atomicAdd(&counts[2], bad_div);
+    if (checked) atomicAdd(&counts[3], checked);
+}
+
 // ---------------------------------------------------------------- host side
 
 static int device_sms() {
@@ -568,6 +626,24 @@ int smo_selftest_wait_timeout(void *workspace, size_t workspace_bytes, int64_t m
     }
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(status_out, flag + 1, sizeof(int32_t), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e == cudaSuccess ? SMO_OK : cuda_fail(e);
+}
+
+int smo_selftest_fastmath(void *workspace, size_t workspace_bytes, uint64_t n_pairs, uint64_t *counts_out,
+                          void *stream_ptr) {
+    if (!counts_out) return SMO_ERR_INVALID;
+    if (!workspace || workspace_bytes < kWsHeader || !aligned(workspace, kScratchAlign)) return SMO_ERR_WORKSPACE;
+    cudaStream_t stream = (cudaStream_t)stream_ptr;
+    // header bytes 160..191 hold the four counters; a later step's words are untouched
+    unsigned long long *counts = (unsigned long long *)((char *)workspace + 160);
+    cudaError_t e = cudaMemsetAsync(counts, 0, 4 * sizeof(unsigned long long), stream);
+    if (e == cudaSuccess) {
+        selftest_fastmath_kernel<<<device_sms() * 8, 256, 0, stream>>>(n_pairs, counts);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(counts_out, counts, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     return e == cudaSuccess ? SMO_OK : cuda_fail(e);
 }

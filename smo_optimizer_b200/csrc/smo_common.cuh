@@ -38,6 +38,71 @@ __device__ __forceinline__ float adam_write(float p, float m, float v, const smo
     return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
 }
 
+// ---------------------------------------------------------------- FMA-only sqrt and division
+//
+// Hardware approximations refined by FMA corrections (P. Markstein,
+// "Computation of elementary functions on the IBM RISC System/6000
+// processor", IBM J. Res. Dev. 34(1), 1990; Muller et al., Handbook of
+// Floating-Point Arithmetic, chapters on Newton-Raphson based division and
+// square root).  Each sequence is exact (bit-identical to the IEEE operation)
+// only on a stated input range; smo_selftest_fastmath() checks those ranges
+// on the device: every input for the square root and the reciprocal,
+// pseudo-random pairs for the quotient.
+
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// NaN-propagating min / max (PTX min.NaN / max.NaN)
+__device__ __forceinline__ float nan_min(float a, float b) {
+    float y;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+    return y;
+}
+
+__device__ __forceinline__ float nan_max(float a, float b) {
+    float y;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(y) : "f"(a), "f"(b));
+    return y;
+}
+
+// sqrt of each lane: s = v y, h = y / 2 (y ~ 1/sqrt(v)), then s + (v - s s) h.
+// Equals the correctly rounded square root for every finite v >= 2^-102;
+// +0 and +inf give NaN.
+__device__ __forceinline__ float2 sqrt2_markstein(float2 v) {
+    const float2 y = make_float2(rsqrt_approx(v.x), rsqrt_approx(v.y));
+    const float2 s = __fmul2_rn(v, y), h = __fmul2_rn(make_float2(0.5f, 0.5f), y);
+    const float2 r = __ffma2_rn(make_float2(-s.x, -s.y), s, v);
+    return __ffma2_rn(r, h, s);
+}
+
+// reciprocal of each lane by one Newton step from the approximation; equals
+// RN(1/d) for every normal d in [2^-126, 2^126]
+__device__ __forceinline__ float2 rcp2_newton(float2 d) {
+    const float2 r0 = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+    const float2 e = __ffma2_rn(make_float2(-d.x, -d.y), r0, make_float2(1.0f, 1.0f));
+    return __ffma2_rn(r0, e, r0);
+}
+
+// a / d per lane with r = RN(1/d): q0 = RN(a r), rem = a - d q0 (exact by
+// FMA), q = RN(q0 + rem r).  By Markstein's theorem q is the correctly rounded
+// quotient when d is normal, q0 is within an ulp of a/d and nothing under- or
+// overflows; for d >= 2^-27 that holds whenever |q0| is in [2^-76, 2^100]
+// (then exponent(d) + exponent(q0) >= -103 keeps rem representable).
+__device__ __forceinline__ float2 div2_markstein(float2 a, float2 d, float2 r, float2 &q0) {
+    q0 = __fmul2_rn(a, r);
+    const float2 rem = __ffma2_rn(make_float2(-q0.x, -q0.y), d, a);
+    return __ffma2_rn(rem, r, q0);
+}
+
 // torch.clamp(v, min=0): NaN passes through (fmaxf would drop it)
 __device__ __forceinline__ float clamp_min0(float v) { return v < 0.0f ? 0.0f : v; }
 

@@ -193,7 +193,8 @@ __device__ __forceinline__ float2 div_rcp2(float2 x, float2 c, float2 r) {
 // p + ((-lr/bc1) * m) / (sqrt(v)/sqrt(bc2) + eps).  sqrt(v) is 0, normal, +inf
 // or NaN and sqrt(bc2) is in (0, 1], so the divide-by-constant stays normal.
 struct AdamK {
-    float2 sbc2, rcp_sbc2, eps, ns;
+    float2 sbc2, neg_sbc2, rcp_sbc2, eps, ns;
+    bool fast;  // eps >= 2^-27: the denominator is >= 2^-27 (or not finite)
 };
 
 __device__ __forceinline__ float2 adam_write2(float2 p, float2 m, float2 v, const AdamK &k) {
@@ -201,6 +202,24 @@ __device__ __forceinline__ float2 adam_write2(float2 p, float2 m, float2 v, cons
     const float2 d = __fadd2_rn(div_rcp2(sv, k.sbc2, k.rcp_sbc2), k.eps);
     const float2 a = __fmul2_rn(k.ns, m);
     return __fadd2_rn(p, f2(__fdiv_rn(a.x, d.x), __fdiv_rn(a.y, d.y)));
+}
+
+// The same write with FMA-only arithmetic (sqrt2_markstein, Markstein's
+// division by sqrt(bc2) and div2_markstein).  Returns false unless v >= 2^-100
+// and |q0| is in [2^-76, 2^100] in both lanes, the ranges where every step is
+// exact (zero, tiny, non-finite and NaN inputs all fail); the caller then
+// redoes the pair with adam_write2.
+__device__ __forceinline__ bool adam_write2_fast(float2 p, float2 m, float2 v, const AdamK &k, float2 &out) {
+    const float2 sv = sqrt2_markstein(v);
+    const float2 t0 = __fmul2_rn(sv, k.rcp_sbc2);
+    const float2 d = __fadd2_rn(__ffma2_rn(__ffma2_rn(t0, k.neg_sbc2, sv), k.rcp_sbc2, t0), k.eps);
+    const float2 a = __fmul2_rn(k.ns, m);
+    float2 q0;
+    const float2 q = div2_markstein(a, d, rcp2_newton(d), q0);
+    out = __fadd2_rn(p, q);
+    const float lo = nan_min(__fmul_rn(nan_min(v.x, v.y), 0x1p24f), nan_min(fabsf(q0.x), fabsf(q0.y)));
+    const float hi = nan_max(fabsf(q0.x), fabsf(q0.y));
+    return lo >= 0x1p-76f && hi <= 0x1p100f;
 }
 
 // codes * (scales / 127) for an (m, v) pair; scales >= 1e-12 (clamped block
@@ -226,20 +245,6 @@ __device__ __forceinline__ int8_t quantize_rc(float x, float s, float rs) {
     r = r > 127.0f ? 127.0f : r;
     r = r < -127.0f ? -127.0f : r;
     return (r == r) ? (int8_t)(int)r : (int8_t)0;
-}
-
-// Hint the next compact row's gradient and parameter rows into L2 (TMA bulk
-// prefetch; no shared memory, no completion to wait for).
-template <int KH>
-__device__ __forceinline__ void prefetch_row_l2(const FusedDesc &d, int c) {
-    const int i = threadIdx.x;
-    if (i < 2 * KH) {
-        const float *base = (i < KH ? d.g : d.p) + ((int64_t)c * KH + (i % KH)) * d.W;
-        if (i >= KH && !d.hp.wd_on) return;
-        const uint32_t bytes = (uint32_t)((d.W * 4) & ~(int64_t)15);
-        if (((uintptr_t)base & 15) == 0 && bytes > 0)
-            asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base), "r"(bytes) : "memory");
-    }
 }
 
 // ---------------------------------------------------------------- phases
@@ -387,9 +392,67 @@ __device__ __forceinline__ float col_l1(int t) {
     return (t + 0.5f) / KW + (t < KW / 2 ? 0.5f : -0.5f);
 }
 
+// Width pass of the three compact rows at column j: the left half of the
+// window interpolates columns (j-1, j), the right half (j, j+1), clamped at
+// the edges exactly as torch's index/lambda computation does
+template <int KW>
+__device__ __forceinline__ void width_pass3(const float2 *const R[3], int j, int w, float2 (&h)[3][KW]) {
+    const int jr = j + 1 < w ? j + 1 : w - 1;
+    const int la = j > 0 ? j - 1 : 0;
+#pragma unroll
+    for (int s = 0; s < 3; s++) {
+        const float2 left = R[s][la], mid = R[s][j], right = R[s][jr];
+        const float2 x = j > 0 ? mid : right;
+#pragma unroll
+        for (int t = 0; t < KW; t++) {
+            if (t < KW / 2) {
+                const float l1 = j > 0 ? col_l1<KW>(t) : 0.0f;
+                const float l0 = j > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
+                h[s][t] = __ffma2_rn(left, splat(l0), __fmul2_rn(x, splat(l1)));
+            } else {
+                h[s][t] = __ffma2_rn(mid, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(right, splat(col_l1<KW>(t))));
+            }
+        }
+    }
+}
+
+// Rows of cell j (bits of `rows`) whose fast Adam write failed its range
+// check: recomputed with the IEEE operations from the untouched parameters.
+template <int KH, int KW>
+__device__ __noinline__ void phase2_fixup(const FusedDesc &d, int c, int j, const float2 *const R[3],
+                                          const RowCo *rowco, const AdamK &ak, unsigned rows) {
+    const int64_t W = d.W;
+    float2 h[3][KW];
+    width_pass3<KW>(R, j, d.w, h);
+    for (int i = 0; i < KH; i++) {
+        if (!((rows >> i) & 1u)) continue;
+        float *prow = d.p + ((int64_t)c * KH + i) * W + (int64_t)j * KW;
+        float pv[KW];
+        load_param_row<KW, true>(prow, pv);
+        const RowCo rc = rowco[i];
+#pragma unroll
+        for (int t = 0; t < KW; t += 2) {
+            float2 m2[2];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float2 a = rc.s0 == 0 ? h[0][t + e] : h[1][t + e];
+                const float2 b = rc.s1 == 1 ? h[1][t + e] : h[2][t + e];
+                m2[e] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
+            }
+            const float2 pn = adam_write2(f2(pv[t], pv[t + 1]), f2(m2[0].x, m2[1].x),
+                                          f2(clamp_min0(m2[0].y), clamp_min0(m2[1].y)), ak);
+            pv[t] = pn.x;
+            pv[t + 1] = pn.y;
+        }
+        store_param_row<KW>(prow, pv);
+    }
+}
+
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
 // c-1 (R[0]), c (R[1]), c+1 (R[2]) in shared memory (an absent neighbour row
 // is passed as row c and never weighted).  Row weights come from `rowco`.
+// Every element takes the FMA-only Adam write; a row whose range check fails
+// is not stored and goes to phase2_fixup.
 template <int KH, int KW, int NT>
 __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
                                        const AdamK &ak) {
@@ -400,27 +463,9 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
         float pv[KH][KW];
 #pragma unroll
         for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
-        // width pass of the three compact rows: the left half of the window
-        // interpolates columns (j-1, j), the right half (j, j+1), clamped at the
-        // edges exactly as torch's index/lambda computation does
-        const int jr = j + 1 < w ? j + 1 : w - 1;
-        const int la = j > 0 ? j - 1 : 0;
         float2 h[3][KW];
-#pragma unroll
-        for (int s = 0; s < 3; s++) {
-            const float2 left = R[s][la], mid = R[s][j], right = R[s][jr];
-            const float2 x = j > 0 ? mid : right;
-#pragma unroll
-            for (int t = 0; t < KW; t++) {
-                if (t < KW / 2) {
-                    const float l1 = j > 0 ? col_l1<KW>(t) : 0.0f;
-                    const float l0 = j > 0 ? 1.0f - col_l1<KW>(t) : 1.0f;
-                    h[s][t] = __ffma2_rn(left, splat(l0), __fmul2_rn(x, splat(l1)));
-                } else {
-                    h[s][t] = __ffma2_rn(mid, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(right, splat(col_l1<KW>(t))));
-                }
-            }
-        }
+        width_pass3<KW>(R, j, w, h);
+        unsigned fail = 0;
 #pragma unroll
         for (int i = 0; i < KH; i++) {
             const RowCo rc = rowco[i];
@@ -432,15 +477,20 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
                 const float2 b = lo1 ? h[1][t] : h[2][t];
                 mh[t] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
             }
+            bool ok = ak.fast;
+            float pn[KW];
 #pragma unroll
             for (int t = 0; t < KW; t += 2) {
-                const float2 pn = adam_write2(f2(pv[i][t], pv[i][t + 1]), f2(mh[t].x, mh[t + 1].x),
-                                              f2(clamp_min0(mh[t].y), clamp_min0(mh[t + 1].y)), ak);
-                pv[i][t] = pn.x;
-                pv[i][t + 1] = pn.y;
+                float2 o;
+                ok &= adam_write2_fast(f2(pv[i][t], pv[i][t + 1]), f2(mh[t].x, mh[t + 1].x),
+                                       f2(clamp_min0(mh[t].y), clamp_min0(mh[t + 1].y)), ak, o);
+                pn[t] = o.x;
+                pn[t + 1] = o.y;
             }
-            store_param_row<KW>(pbase + i * W, pv[i]);
+            if (ok) store_param_row<KW>(pbase + i * W, pn);
+            else fail |= 1u << i;
         }
+        if (fail) phase2_fixup<KH, KW>(d, c, j, R, rowco, ak, fail);
     }
 }
 
@@ -457,9 +507,11 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
     AdamK ak;
     ak.sbc2 = splat(d.hp.sqrt_bc2);
+    ak.neg_sbc2 = splat(-d.hp.sqrt_bc2);
     ak.rcp_sbc2 = splat(__frcp_rn(d.hp.sqrt_bc2));
     ak.eps = splat(d.hp.eps);
     ak.ns = splat(d.hp.neg_step);
+    ak.fast = d.hp.eps >= 0x1p-27f;
     auto RR = [&](int c) { return ring + (c % 3) * w; };
     float2 *pub = reinterpret_cast<float2 *>(halo + d.halo_off) + (int64_t)sidx * w;
     // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
@@ -473,7 +525,6 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     for (int r = c0; r <= last; r++) {
         const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
         if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
-        if (r < last) prefetch_row_l2<KH>(d, r + 1);
         phase1<KH, KW, CELLS, NT>(d, r, RR(r), r < c1);
         __syncthreads();
         if (r < c1) {
@@ -560,8 +611,8 @@ __global__ void __launch_bounds__(NT, MINB)
         __syncthreads();
         if (s >= total) break;
         const int t = find_strip_tensor(b, s);
-        process_strip<KH, KW, CELLS, NT>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags, halo,
-                              wait_iters);
+        process_strip<KH, KW, CELLS, NT>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags,
+                                         halo, wait_iters);
     }
     if (threadIdx.x == 0) {
         __threadfence();

@@ -99,6 +99,22 @@ def test_bounded_wait_times_out_and_context_survives():
     assert float(x.sum().item()) == 1000.0
 
 
+def test_fastmath_selftest_matches_ieee():
+    """The fused step's FMA-only sqrt (every finite v >= 2^-102), reciprocal
+    (every normal d in [2^-126, 2^126]) and 2^31 random in-range quotients
+    equal the IEEE results bit for bit."""
+    import ctypes
+    lib = _lib.load()
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    counts = (ctypes.c_uint64 * 4)()
+    _lib.check(lib.smo_selftest_fastmath(ws.data_ptr(), ws.numel(), 1 << 31, counts,
+                                         torch.cuda.current_stream().cuda_stream), "selftest_fastmath")
+    assert counts[0] == 0, f"{counts[0]} square roots differ"
+    assert counts[1] == 0, f"{counts[1]} reciprocals differ"
+    assert counts[2] == 0, f"{counts[2]} quotients differ"
+    assert counts[3] > (1 << 31)
+
+
 # ------------------------------------------------------------------ full steps
 
 def run_gpu_case(name, steps=None, general=False):
@@ -227,3 +243,35 @@ def test_fused_random_shapes_vs_oracle(H, W, k, block, band_mb, wd):
     for key in ("m_q", "m_s", "v_q", "v_s"):
         assert np.array_equal(host(st[key]).reshape(-1), rst[key].reshape(-1)), key
     assert np.array_equal(host(p), ref_p)
+
+
+@pytest.mark.parametrize("eps", [1e-8, 1e-12])
+def test_fused_ieee_fallback_rows_vs_oracle(eps):
+    """Zero, tiny and huge gradient regions send rows of the fused kernel's
+    FMA-only Adam write to its IEEE fix-up (eps < 2^-27 sends every row); the
+    result stays bit-identical to the oracle."""
+    H, W = 4 * 40, 4 * 384
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), eps=eps, weight_decay=0.01, k_ratio=0.25, block_size=64,
+              low_peak=True, band_mb=0.5)
+    p0 = synthetic.synth_param(8, 0, (H, W))
+    p = torch.nn.Parameter(cuda(p0))
+    opt = SMO8bit([p], **kw)
+    ref_p = p0.copy()
+    ref = oracle.OracleOptimizer("SMO8bit", [{"params": [ref_p]}], **kw)
+    for step in range(1, 4):
+        g = synthetic.synth_grad(8, step, 0, (H, W)).copy()
+        g[8:40, :] = 0.0                      # whole zero rows: m = v = 0 there
+        g[40:72, 64:512] = 0.0                # a zero patch inside rows
+        g[72:104, 512:1024] *= 1e-28          # tiny: v far below 2^-100
+        g[104:120, 1024:1280] *= 1e12         # huge values
+        if step == 2:
+            g[120:136, :256] = 0.0            # a region that turns zero later
+        p.grad = cuda(g)
+        opt.step()
+        ref.step([g])
+    torch.cuda.synchronize()
+    assert opt.workspace_status() == 0
+    st, rst = opt.state[p], ref.state[(0, 0)]
+    for key in ("m_q", "m_s", "v_q", "v_s"):
+        assert np.array_equal(host(st[key]).reshape(-1), rst[key].reshape(-1)), key
+    assert np.array_equal(host(p).view(np.uint32), ref_p.view(np.uint32))
