@@ -43,7 +43,7 @@ namespace smo {
 
 constexpr int kMaxFusedCtasPerSm = 4;
 constexpr int kMaxFused = 104;
-constexpr int64_t kStripRows = 16;          // target compact rows per strip
+constexpr int64_t kStripRows = 16;          // longest strip (compact rows); shorter when a launch has few
 constexpr int64_t kMaxFusedCols = 8192;     // compact columns (shared memory: 24 B per column)
 constexpr int64_t kDefaultWaitIters = 1 << 22;
 
@@ -650,10 +650,12 @@ static FastDiv make_fast_div(uint32_t d) {
     return f;
 }
 
-static int64_t strip_rows(const smo_tensor &t) {
+// Compact rows per strip for a target length: a multiple of the rows after
+// which int8 blocks realign with row starts, at most the tensor's rows.
+static int64_t strip_rows(const smo_tensor &t, int64_t target) {
     int64_t align = 1;
     if (t.kind == SMO_KIND_POOLED8) align = t.q_block / gcd64(t.comp_cols, t.q_block);
-    int64_t L = (kStripRows + align - 1) / align * align;
+    int64_t L = (target + align - 1) / align * align;
     return L < t.comp_rows ? L : t.comp_rows;
 }
 
@@ -683,8 +685,8 @@ bool fused_takes(const smo_tensor &t) {
     return true;
 }
 
-static int64_t num_strips(const smo_tensor &t) {
-    const int64_t L = strip_rows(t);
+static int64_t num_strips(const smo_tensor &t, int64_t target) {
+    const int64_t L = strip_rows(t, target);
     return (t.comp_rows + L - 1) / L;
 }
 
@@ -721,23 +723,67 @@ static int device_sm_count() {
 
 static inline size_t align_up(size_t x) { return (x + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
 
+// Launch plan: tensors the fused kernel takes, grouped by window shape in scan
+// order (at most kMaxFused per launch), each group with its strip length.
+// Short launches get shorter strips so that every CTA slot sees several
+// strips (the last strips of a launch otherwise leave SMs idle): the longest
+// of 16, 8, 4 rows that gives at least 4 strips per CTA slot of a 2-CTA/SM
+// grid.
+struct LaunchGroup {
+    int key;
+    int64_t target_rows;
+    std::vector<int32_t> members;
+};
+
+static int device_sm_count();
+
+static void plan_launches(const smo_tensor *t, int32_t n, std::vector<LaunchGroup> &out) {
+    out.clear();
+    std::vector<char> done((size_t)n);
+    for (int32_t i = 0; i < n; i++) done[i] = !fused_takes(t[i]);
+    const int64_t want = 4 * 2 * (int64_t)device_sm_count();
+    for (int32_t i = 0; i < n; i++) {
+        if (done[i]) continue;
+        LaunchGroup g;
+        g.key = window_key(t[i]);
+        for (int32_t k = i; k < n && (int)g.members.size() < kMaxFused; k++) {
+            if (done[k] || window_key(t[k]) != g.key) continue;
+            g.members.push_back(k);
+            done[k] = 1;
+        }
+        g.target_rows = kStripRows;
+        while (g.target_rows > 4) {
+            int64_t strips = 0;
+            for (int32_t k : g.members) strips += num_strips(t[k], g.target_rows);
+            if (strips >= want) break;
+            g.target_rows /= 2;
+        }
+        out.push_back(std::move(g));
+    }
+}
+
 // Workspace after the header: [flags: one word per strip][published rows:
 // 2*w floats per strip][head rows: 4*max_w floats per CTA].  Sized for the
 // whole set; each window-group launch reuses the space.
 size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
-    size_t strips = 0, halo_floats = 0;
-    int64_t max_w = 0;
-    for (int32_t i = 0; i < n; i++) {
-        if (!fused_takes(t[i])) continue;
-        const int64_t s = num_strips(t[i]);
-        strips += (size_t)s;
-        halo_floats += (size_t)s * 2 * (size_t)t[i].comp_cols;
-        max_w = max_w > t[i].comp_cols ? max_w : t[i].comp_cols;
-    }
-    if (!strips) return 0;
+    std::vector<LaunchGroup> groups;
+    plan_launches(t, n, groups);
+    size_t need = 0;
     const size_t ctas = (size_t)device_sm_count() * kMaxFusedCtasPerSm;
-    return align_up(strips * sizeof(unsigned int)) + align_up(halo_floats * sizeof(float)) +
-           ctas * 4 * (size_t)max_w * sizeof(float);
+    for (const LaunchGroup &g : groups) {
+        size_t strips = 0, halo_floats = 0;
+        int64_t max_w = 0;
+        for (int32_t k : g.members) {
+            const int64_t s = num_strips(t[k], g.target_rows);
+            strips += (size_t)s;
+            halo_floats += (size_t)s * 2 * (size_t)t[k].comp_cols;
+            max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
+        }
+        const size_t bytes = align_up(strips * sizeof(unsigned int)) + align_up(halo_floats * sizeof(float)) +
+                             ctas * 4 * (size_t)max_w * sizeof(float);
+        need = need > bytes ? need : bytes;
+    }
+    return need;
 }
 
 // The kernel instance of a window shape and CTA width: 16-element windows take
@@ -791,7 +837,7 @@ static int dispatch(int key, FusedBatch &b, int64_t max_w, size_t halo_floats, c
     }
 }
 
-static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off) {
+static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off, int64_t target_rows) {
     memset(&f, 0, sizeof(f));
     f.p = t.param;
     f.g = t.grad;
@@ -801,7 +847,7 @@ static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off) {
     f.H = t.rows; f.W = t.cols; f.band = t.interp_band;
     f.h = (int32_t)t.comp_rows; f.w = (int32_t)t.comp_cols;
     f.B = t.kind == SMO_KIND_POOLED8 ? (int32_t)t.q_block : 1;
-    f.L = (int32_t)strip_rows(t);
+    f.L = (int32_t)strip_rows(t, target_rows);
     f.div_B = make_fast_div((uint32_t)f.B);
     f.div_w = make_fast_div((uint32_t)f.w);
     f.halo_off = halo_off;
@@ -812,29 +858,24 @@ static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off) {
 int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaStream_t stream) {
     (void)ws_bytes;
     static thread_local FusedBatch batch;
-    // one launch per window shape (template instance), at most kMaxFused tensors each
-    std::vector<char> done((size_t)n);
-    for (int32_t i = 0; i < n; i++) done[i] = !fused_takes(t[i]);
-    for (int32_t i = 0; i < n; i++) {
-        if (done[i]) continue;
-        const int key = window_key(t[i]);
+    static thread_local std::vector<LaunchGroup> groups;
+    plan_launches(t, n, groups);
+    // one launch per group (window shape, at most kMaxFused tensors); the
+    // groups run one after another and reuse the workspace
+    for (const LaunchGroup &g : groups) {
         batch.n = 0;
         batch.strip_start[0] = 0;
         int64_t halo_off = 0, max_w = 0;
-        for (int32_t k = i; k < n && batch.n < kMaxFused; k++) {
-            if (done[k] || window_key(t[k]) != key) continue;
+        for (int32_t k : g.members) {
             FusedDesc &f = batch.d[batch.n];
-            fill(f, t[k], halo_off);
-            const int64_t s = num_strips(t[k]);
+            fill(f, t[k], halo_off, g.target_rows);
+            const int64_t s = num_strips(t[k], g.target_rows);
             halo_off += s * 2 * t[k].comp_cols;
             max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
             batch.strip_start[batch.n + 1] = batch.strip_start[batch.n] + s;
             batch.n++;
-            done[k] = 1;
         }
-        // tensors of the same window left over (batch full) start a new batch when
-        // the scan reaches them
-        const int st = dispatch(key, batch, max_w, (size_t)halo_off, ws, stream);
+        const int st = dispatch(g.key, batch, max_w, (size_t)halo_off, ws, stream);
         if (st != SMO_OK) return st;
     }
     return SMO_OK;

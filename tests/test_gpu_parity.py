@@ -222,6 +222,8 @@ def test_fused_kernel_matches_general_kernels(name):
     (2 * 50, 2 * 700, 0.5, 64, 0.0, 0.01),      # 2x2 windows
     (8 * 21, 8 * 40, 0.125, 20, 0.0, 0.01),     # 8x8 windows, block 20
     (32, 4 * 1024, 0.25, 64, 0.0, 0.01),        # one strip of 8 compact rows, 4 columns per thread
+    (4 * 20, 4 * 1152, 0.25, 64, 0.5, 0.01),    # 384-thread CTAs, 3 columns per thread, bands
+    (4 * 37, 4 * 512, 0.25, 128, 0.0, 0.0),     # 256-thread CTAs, 128-cell blocks, no weight decay
 ])
 def test_fused_random_shapes_vs_oracle(H, W, k, block, band_mb, wd):
     kw = dict(lr=2e-3, betas=(0.8, 0.99), eps=1e-8, weight_decay=wd, k_ratio=k, block_size=block)
@@ -274,4 +276,28 @@ def test_fused_ieee_fallback_rows_vs_oracle(eps):
     st, rst = opt.state[p], ref.state[(0, 0)]
     for key in ("m_q", "m_s", "v_q", "v_s"):
         assert np.array_equal(host(st[key]).reshape(-1), rst[key].reshape(-1)), key
+    assert np.array_equal(host(p).view(np.uint32), ref_p.view(np.uint32))
+
+
+def test_fused_fp32_moments_4x4_vs_oracle():
+    """SMO (fp32 pooled moments) on 4x4 windows through the fused kernel
+    (384-thread CTAs, two columns per thread); bit-identical to the oracle
+    over three steps."""
+    H, W = 4 * 24, 4 * 768
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, k_ratio=0.25)
+    p0 = synthetic.synth_param(9, 0, (H, W))
+    p = torch.nn.Parameter(cuda(p0))
+    opt = SMO([p], **kw)
+    ref_p = p0.copy()
+    ref = oracle.OracleOptimizer("SMO", [{"params": [ref_p]}], **kw)
+    for step in range(1, 4):
+        g = synthetic.synth_grad(9, step, 0, (H, W))
+        p.grad = cuda(g)
+        opt.step()
+        ref.step([g])
+    torch.cuda.synchronize()
+    assert opt.workspace_status() == 0
+    st, rst = opt.state[p], ref.state[(0, 0)]
+    for key in ("exp_avg", "exp_avg_sq"):
+        assert np.array_equal(host(st[key]).reshape(-1), np.asarray(rst[key]).reshape(-1)), key
     assert np.array_equal(host(p).view(np.uint32), ref_p.view(np.uint32))
