@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define SMO_ABI_VERSION 1
+#define SMO_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define SMO_API __attribute__((visibility("default")))
@@ -100,6 +100,12 @@ typedef struct smo_tensor {
     int32_t kind;                   /* smo_kind */
     int32_t flags;                  /* SMO_FLAG_* (0 = let the library choose the kernel) */
     smo_hyper hp;
+    /* permute_basis (spatial_8bit.py:202-204, 231-253; pooled kinds, monolithic
+       interpolation): the gradient is pooled in the basis whose row i is view
+       row row_perm[i] and column j is view column col_perm[j], and the
+       reconstructed moments are mapped back with the inverse permutations
+       (row_perm_inv[row_perm[i]] = i).  All four null = no permutation. */
+    const int64_t *row_perm, *col_perm, *row_perm_inv, *col_perm_inv;
 } smo_tensor;
 
 /* ---- the optimizer step ------------------------------------------------ */

@@ -162,8 +162,11 @@ class OracleOptimizer:
     """
 
     def __init__(self, kind, groups, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
-                 k_ratio=0.25, block_size=64, low_peak=False, band_mb=64.0, compress_conv=False):
+                 k_ratio=0.25, block_size=64, low_peak=False, band_mb=64.0, compress_conv=False,
+                 permute_basis=False):
         assert kind in ("SMO8bit", "SMO")
+        if low_peak and permute_basis:
+            raise ValueError("permute_basis is not supported with low_peak")
         self.kind = kind
         self.defaults = dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, k_ratio=k_ratio,
                              block_size=block_size)
@@ -175,6 +178,11 @@ class OracleOptimizer:
         self.low_peak = low_peak
         self.band_mb = float(band_mb)
         self.compress_conv = bool(compress_conv)
+        self.permute_basis = bool(permute_basis) and kind == "SMO8bit"
+        # permute_basis: (row_perm, col_perm) per state key, placed before the
+        # first step (the reference draws them with torch.randperm,
+        # spatial_8bit.py:202-204); absent keys get a seeded numpy permutation
+        self.preset_perms = {}
         self.state = {}
 
     def params(self):
@@ -182,7 +190,7 @@ class OracleOptimizer:
             for pi, p in enumerate(g["params"]):
                 yield (gi, pi), g, p
 
-    def _init(self, p, group):
+    def _init(self, p, group, key=None):
         raw = group.get("compress", True)
         quant_only = (raw == "quant_only")
         st = {"step": 0}
@@ -207,6 +215,11 @@ class OracleOptimizer:
                 st["m_q"], st["m_s"] = quantize(z, st["q_block"])
                 st["v_q"], st["v_s"] = quantize(z, st["q_block"])
                 st["comp_shape"] = cs
+                if self.permute_basis:
+                    rp, cp = self.preset_perms.get(key) or (np.random.default_rng(0).permutation(vshape[0]),
+                                                             np.random.default_rng(1).permutation(vshape[1]))
+                    st["row_perm"] = np.asarray(rp, np.int64)
+                    st["col_perm"] = np.asarray(cp, np.int64)
             else:
                 st["exp_avg"] = np.zeros(cs, np.float32)
                 st["exp_avg_sq"] = np.zeros(cs, np.float32)
@@ -223,7 +236,7 @@ class OracleOptimizer:
                 continue
             st = self.state.get(key)
             if st is None:
-                st = self.state[key] = self._init(p, group)
+                st = self.state[key] = self._init(p, group, key)
             st["step"] += 1
             sc = _host.step_scalars(group["lr"], group["betas"], group["eps"], group["weight_decay"],
                                     st["step"])
@@ -237,7 +250,15 @@ class OracleOptimizer:
                     band = 0
                     if self.low_peak and _host.can_band(st["orig_shape"], st["comp_shape"]):
                         band = _host.band_comp_rows(st["orig_shape"], st["comp_shape"], self.band_mb)
-                    smo8bit_pooled_step(p2, g2, st, sc, band)
+                    if "row_perm" in st:
+                        # the step in the permuted basis (spatial_8bit.py:231-253): pool
+                        # g[rp][:, cp], reconstruct there, map the update back
+                        ix = np.ix_(st["row_perm"], st["col_perm"])
+                        pp = np.ascontiguousarray(p2[ix])
+                        smo8bit_pooled_step(pp, np.ascontiguousarray(g2[ix]), st, sc, band)
+                        p2[ix] = pp
+                    else:
+                        smo8bit_pooled_step(p2, g2, st, sc, band)
                 else:
                     smo_pooled_step(p2, g2, st, sc)
             else:

@@ -19,7 +19,7 @@ SMO_KIND_POOLED32 = 2
 SMO_KIND_DENSE = 3
 SMO_KIND_QUANT_ONLY = 4
 SMO_ERR_TIMEOUT = 5
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # Field layout of struct smo_hyper / smo_tensor, as a numpy structured dtype so
 # that descriptor tables are filled column-wise without per-field Python calls.
@@ -38,6 +38,7 @@ TENSOR_DTYPE = np.dtype([
     ("q_block", np.int64), ("interp_band", np.int64),
     ("kind", np.int32), ("flags", np.int32),
     ("hp", HYPER_DTYPE),
+    ("row_perm", np.uint64), ("col_perm", np.uint64), ("row_perm_inv", np.uint64), ("col_perm_inv", np.uint64),
 ])
 
 HYPER_FIELDS = HYPER_DTYPE.names

@@ -60,7 +60,7 @@ __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
         if (c >= C) break;
         int64_t i = c / d.w, j = c - i * d.w;
         float gm, g2;
-        pool_cell(d.g, d.p, d.H, d.W, d.h, d.w, d.exact, i, j, hp, gm, g2);
+        pool_cell(d.g, d.p, d.H, d.W, d.h, d.w, d.exact, i, j, hp, gm, g2, d.rp, d.cp);
         float m, v;
         if (q8) {
             m = dequant1(d.mq_in[c], tm);
@@ -179,22 +179,26 @@ __global__ void __launch_bounds__(256) step_b_kernel(const __grid_constant__ Bat
         const int t = find_tensor(b.start_b, b.n, it);
         const DevDesc &d = b.d[t];
         const int64_t r = it - b.start_b[t];
+        // permute_basis: parameter row r / column q sit at row rpi[r] / column
+        // cpi[q] of the basis the moments were reconstructed in
+        const int64_t br = d.rpi ? d.rpi[r] : r;
         int small;
-        const Coef rc = row_coef(r, d.H, d.h, d.W, d.band, small);
+        const Coef rc = row_coef(br, d.H, d.h, d.W, d.band, small);
         float *prow = d.p + r * d.W;
         for (int64_t q = lane; q < d.W; q += 32) {
+            const int64_t bq = d.cpi ? d.cpi[q] : q;
             float mh, vh;
             if (d.same) {
-                mh = d.m_out[r * d.w + q];
-                vh = d.v_out[r * d.w + q];
+                mh = d.m_out[br * d.w + bq];
+                vh = d.v_out[br * d.w + bq];
             } else {
-                const Coef cc = coef_for(q, d.w, d.W);
+                const Coef cc = coef_for(bq, d.w, d.W);
                 if (small) {
                     mh = interp_small(d.m_out, d.w, rc, cc);
                     vh = interp_small(d.v_out, d.w, rc, cc);
                 } else {
-                    mh = interp_generic(d.m_out, d.w, rc, cc, r, q);
-                    vh = interp_generic(d.v_out, d.w, rc, cc, r, q);
+                    mh = interp_generic(d.m_out, d.w, rc, cc, br, bq);
+                    vh = interp_generic(d.v_out, d.w, rc, cc, br, bq);
                 }
             }
             prow[q] = adam_write(prow[q], mh, clamp_min0(vh), d.hp);
@@ -357,6 +361,9 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
     memset(&d, 0, sizeof(d));
     if (!t.param || !t.grad) return SMO_ERR_INVALID;
     if (!aligned(t.param, 4) || !aligned(t.grad, 4)) return SMO_ERR_ALIGNMENT;
+    const int nperm = (t.row_perm != nullptr) + (t.col_perm != nullptr) + (t.row_perm_inv != nullptr) +
+                      (t.col_perm_inv != nullptr);
+    if (nperm && t.kind != SMO_KIND_POOLED8 && t.kind != SMO_KIND_POOLED32) return SMO_ERR_INVALID;
     d.p = t.param;
     d.g = t.grad;
     d.kind = t.kind;
@@ -374,6 +381,18 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
             d.band = t.interp_band;
             if (d.band < 0 || (d.band > 0 && !d.exact)) return SMO_ERR_INVALID;
             d.same = (d.h == d.H && d.w == d.W && d.band == 0);
+            if (nperm) {
+                // permute_basis: all four index arrays, monolithic interpolation only
+                // (the reference rejects low_peak with permute_basis, spatial_8bit.py:75-76)
+                if (nperm != 4 || d.band != 0) return SMO_ERR_INVALID;
+                if (!aligned(t.row_perm, 8) || !aligned(t.col_perm, 8) || !aligned(t.row_perm_inv, 8) ||
+                    !aligned(t.col_perm_inv, 8))
+                    return SMO_ERR_ALIGNMENT;
+                d.rp = t.row_perm;
+                d.cp = t.col_perm;
+                d.rpi = t.row_perm_inv;
+                d.cpi = t.col_perm_inv;
+            }
             if (t.kind == SMO_KIND_POOLED8) {
                 if (t.q_block <= 0) return SMO_ERR_INVALID;
                 if (!t.m_q_in || !t.m_s_in || !t.v_q_in || !t.v_s_in || !t.m_q_out || !t.m_s_out || !t.v_q_out ||

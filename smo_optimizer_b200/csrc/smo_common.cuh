@@ -219,9 +219,13 @@ __device__ __forceinline__ float interp_small(const float *src, int64_t w, const
 
 // Window sums of x and x*x for compact cell (i, j): sequential row-major from
 // +0 (torch's cpu avg_pool2d / adaptive_avg_pool2d loops), then the divisions.
+// With rp / cp set the window is taken in the permuted basis: its row r and
+// column c are view row rp[r] and column cp[c] (g[rp][:, cp] of
+// spatial_8bit.py:235-237).
 __device__ __forceinline__ void pool_cell(const float *__restrict__ g, const float *__restrict__ p, int64_t H,
                                           int64_t W, int64_t h, int64_t w, int exact, int64_t i, int64_t j,
-                                          const smo_hyper &hp, float &mean, float &sq_mean) {
+                                          const smo_hyper &hp, float &mean, float &sq_mean,
+                                          const int64_t *rp = nullptr, const int64_t *cp = nullptr) {
     int64_t r0, r1, c0, c1;
     if (exact) {
         int64_t kh = H / h, kw = W / w;
@@ -233,9 +237,11 @@ __device__ __forceinline__ void pool_cell(const float *__restrict__ g, const flo
     }
     float s1 = 0.0f, s2 = 0.0f;
     for (int64_t r = r0; r < r1; r++) {
-        const float *gr = g + r * W, *pr = p + r * W;
+        const int64_t vr = rp ? rp[r] : r;
+        const float *gr = g + vr * W, *pr = p + vr * W;
         for (int64_t c = c0; c < c1; c++) {
-            float x = decayed(gr[c], pr[c], hp);
+            const int64_t vc = cp ? cp[c] : c;
+            float x = decayed(gr[vc], pr[vc], hp);
             s1 = __fadd_rn(s1, x);
             s2 = __fadd_rn(s2, __fmul_rn(x, x));
         }

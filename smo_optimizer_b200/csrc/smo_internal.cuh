@@ -38,6 +38,8 @@ struct DevDesc {
     int32_t same;   // identity interpolation (h == H, w == W, monolithic)
     int32_t pad_;
     smo_hyper hp;
+    // permute_basis: pooling basis (rp, cp) and its inverse (rpi, cpi); null = identity
+    const int64_t *rp, *cp, *rpi, *cpi;
 };
 
 // Kernel-parameter batch (__grid_constant__, < 32 KB).

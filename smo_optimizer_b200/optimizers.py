@@ -85,6 +85,7 @@ class _SpatialBase(Optimizer):
         self._spare = {}        # param -> alternate moment buffers (double buffering)
         self._workspace = {}    # device index -> uint8 workspace tensor
         self._hyper_cache = {}
+        self._inv_perm = {}     # param -> (row_perm, col_perm, their inverses) for permute_basis
         # smo_tensor.flags for every tensor (SMO_FLAG_GENERAL_PATH pins the
         # general two-launch kernels; used to cross-check the fused kernel)
         self._kernel_flags = 0
@@ -94,6 +95,7 @@ class _SpatialBase(Optimizer):
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)
         self._spare.clear()
+        self._inv_perm.clear()
 
     def _hyper(self, group, step):
         betas = group["betas"]
@@ -138,7 +140,7 @@ class _SpatialBase(Optimizer):
                     raise TypeError(f"{self._name} (B200 build) supports fp32 parameters and gradients; "
                                     f"got {p.dtype} / {grad.dtype}")
                 state = self.state[p]
-                if len(state) == 0:
+                if "step" not in state:
                     self._init_state(p, grad, group)
                 state["step"] += 1
                 per_dev.setdefault(p.device, []).append((p, grad, state, group))
@@ -216,9 +218,6 @@ class SMO8bit(_SpatialBase):
         self.band_mb = float(band_mb)
         if low_peak and permute_basis:
             raise ValueError("permute_basis is not supported with low_peak")
-        if permute_basis:
-            raise NotImplementedError("permute_basis (the basis-permutation ablation) is not implemented "
-                                      "in the B200 build")
         self.permute_basis = permute_basis
 
     # reference helpers (spatial_8bit.py:81-122), on CUDA tensors
@@ -279,10 +278,34 @@ class SMO8bit(_SpatialBase):
             state["v_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
             state["v_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
             state["comp_shape"] = cs
+            if self.permute_basis:
+                # random basis permutations drawn as the reference does
+                # (spatial_8bit.py:202-204); permutations already placed in the
+                # state before the first step are kept
+                for key, n in (("row_perm", vshape[0]), ("col_perm", vshape[1])):
+                    if key in state:
+                        perm = state[key]
+                        if perm.dtype != torch.int64 or tuple(perm.shape) != (n,):
+                            raise ValueError(f"state['{key}'] must be an int64 permutation of {n} indices")
+                        state[key] = perm.to(dev).contiguous()
+                    else:
+                        state[key] = torch.randperm(n, device=dev)
         else:
             state["is_compressed"] = False
             state["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
             state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+
+    def _perms(self, p, state):
+        """(row_perm, col_perm, row_perm_inv, col_perm_inv) of a permuted-basis tensor."""
+        rp, cp = state["row_perm"], state["col_perm"]
+        cached = self._inv_perm.get(p)
+        if cached is None or cached[0] is not rp or cached[1] is not cp:
+            if rp.device != p.device or cp.device != p.device:
+                rp = state["row_perm"] = rp.to(p.device).contiguous()
+                cp = state["col_perm"] = cp.to(p.device).contiguous()
+            cached = (rp, cp, torch.argsort(rp), torch.argsort(cp))
+            self._inv_perm[p] = cached
+        return cached
 
     def _spares(self, p, state):
         sp = self._spare.get(p)
@@ -312,6 +335,9 @@ class SMO8bit(_SpatialBase):
             if self.low_peak and _host.can_band(state["orig_shape"], state["comp_shape"]):
                 rec["interp_band"] = _host.band_comp_rows(state["orig_shape"], state["comp_shape"],
                                                           self.band_mb, grad.element_size())
+            if "row_perm" in state:
+                for k, t in zip(("row_perm", "col_perm", "row_perm_inv", "col_perm_inv"), self._perms(p, state)):
+                    rec[k] = t.data_ptr()
             sp = self._spares(p, state)
             for k, s in zip(("m_q", "m_s", "v_q", "v_s"), sp):
                 rec[k + "_in"] = state[k].data_ptr()

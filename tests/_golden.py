@@ -15,6 +15,16 @@ def load(name):
     return data, meta
 
 
+def golden_perms(name, n_tensors):
+    """The reference's permute_basis draws of a case: (row_perm, col_perm) or None per tensor."""
+    try:
+        data, _ = load(name)
+    except FileNotFoundError:
+        return [None] * n_tensors
+    return [(data[f"{i}.row_perm"], data[f"{i}.col_perm"]) if f"{i}.row_perm" in data else None
+            for i in range(n_tensors)]
+
+
 def code_mismatch_fraction(a, b):
     a = np.asarray(a).reshape(-1)
     b = np.asarray(b).reshape(-1)

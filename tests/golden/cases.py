@@ -68,6 +68,12 @@ CASES = {
     # 8x8 windows (k = 0.125)
     "s8_256x512_k0125": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.125, block_size=64),
                              tensors=[((256, 512), 0)], steps=3, seed=19),
+    # permute_basis (spatial_8bit.py:202-204, 231-253): an exact-window and an
+    # adaptive tensor pooled in a randomly permuted basis (the reference's
+    # torch.randperm draws, seeded, are stored with the golden state)
+    "s8_perm": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64,
+                                               permute_basis=True),
+                    tensors=[((96, 160), 0), ((50, 70), 0)], steps=3, seed=20),
     # SMO-Spatial fp32 pooled moments
     "smo_96x192_k05": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
                            tensors=[((96, 192), 0), ((192,), 0)], steps=5, seed=13),
@@ -82,7 +88,7 @@ CASES = {
                                  tensors=[((100, 200), 0)], steps=3, seed=17),
 }
 
-STATE_ARRAY_KEYS = ("m_q", "m_s", "v_q", "v_s", "exp_avg", "exp_avg_sq")
+STATE_ARRAY_KEYS = ("m_q", "m_s", "v_q", "v_s", "exp_avg", "exp_avg_sq", "row_perm", "col_perm")
 STATE_META_KEYS = ("step", "is_compressed", "is_quant_only", "orig_shape", "param_shape", "comp_numel",
                    "q_block", "comp_shape", "q_shape", "q_numel")
 

@@ -49,6 +49,7 @@ def main():
         groups = C.case_groups(case, params)
         cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
         opt = cls(groups, **case["kwargs"])
+        torch.manual_seed(case["seed"])  # permute_basis draws its permutations at the first step
         for step in range(1, case["steps"] + 1):
             for p, g in zip(params, C.case_grads(case, step)):
                 p.grad = torch.from_numpy(g.copy())

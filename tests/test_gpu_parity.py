@@ -15,7 +15,7 @@ import pytest
 import torch
 
 import cases as C
-from _golden import code_mismatch_fraction, load
+from _golden import code_mismatch_fraction, golden_perms, load
 from oracle import oracle
 from smo_optimizer_b200 import SMO, SMO8bit, _host, _lib, ops, synthetic
 
@@ -123,6 +123,10 @@ def run_gpu_case(name, steps=None, general=False):
     groups = C.case_groups(case, params)
     cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
     opt = cls(groups, **case["kwargs"])
+    for p, pr in zip(params, golden_perms(name, len(params))):
+        if pr is not None:  # the reference's permute_basis draws, placed before the first step
+            opt.state[p]["row_perm"] = cuda(pr[0])
+            opt.state[p]["col_perm"] = cuda(pr[1])
     if general:
         opt._kernel_flags = 1  # SMO_FLAG_GENERAL_PATH
     for step in range(1, (steps or case["steps"]) + 1):
@@ -140,6 +144,9 @@ def run_oracle_case(name, steps=None):
     groups = C.case_groups(case, params)
     opt = oracle.OracleOptimizer(case["opt"], groups, **case["kwargs"])
     keys = [k for k, _, _ in opt.params()]
+    for k, pr in zip(keys, golden_perms(name, len(keys))):
+        if pr is not None:
+            opt.preset_perms[k] = pr
     for step in range(1, (steps or case["steps"]) + 1):
         opt.step(C.case_grads(case, step))
     return params, [opt.state[k] for k in keys]

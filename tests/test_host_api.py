@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 def test_binding_layout_matches_library():
     lib = _lib.load()
     assert lib.smo_abi_version() == _lib.ABI_VERSION
-    assert lib.smo_tensor_struct_size() == _lib.TENSOR_DTYPE.itemsize == 208
+    assert lib.smo_tensor_struct_size() == _lib.TENSOR_DTYPE.itemsize == 240
 
 
 def test_status_strings_and_host_side_validation():

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import cases as C
-from _golden import code_mismatch_fraction, load
+from _golden import code_mismatch_fraction, golden_perms, load
 from oracle import oracle
 
 CODE_FRAC = 1e-5
@@ -25,6 +25,9 @@ def run_oracle(name):
     kw = dict(case["kwargs"])
     opt = oracle.OracleOptimizer(case["opt"], groups, **kw)
     keys = [k for k, _, _ in opt.params()]
+    for k, pr in zip(keys, golden_perms(name, len(keys))):
+        if pr is not None:
+            opt.preset_perms[k] = pr
     for step in range(1, case["steps"] + 1):
         opt.step(C.case_grads(case, step))
     return case, params, [opt.state[k] for k in keys]
