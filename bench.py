@@ -258,7 +258,10 @@ def main():
     costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64)) for s in shapes]
     owner = zero.lpt_partition(costs, world)
     owned = [o == rank for o in owner]
-    params, grads = build_workload(wl, args.seed, device, owned)
+    # N > 1: every rank holds every gradient (a replicated model's backward), which
+    # the gradient reduce-scatter timing below needs; the local step reads only
+    # the owned ones
+    params, grads = build_workload(wl, args.seed, device, owned if world == 1 else [True] * len(owned))
     flat = None
     if world > 1:
         # ZeRO-1 layout: parameters rebound into one rank-contiguous buffer so the
@@ -355,6 +358,32 @@ def main():
                  "params_per_s": total_params / (zms * 1e-3),
                  "allgather_bytes_per_rank": flat.bytes_per_rank,
                  "allgather_busbw_gbs": flat.bytes_per_rank / (ag_ms * 1e-3) / 1e9}
+        # gradient reduce-scatter (ZeRO-2 communication) + local step + all-gather;
+        # every rank holds the same synthetic gradients, so averaging keeps them
+        flat.bind_grads()
+        grads = [p.grad for p in params]
+        for _ in range(3):
+            flat.reduce_scatter_grads()
+            opt.step()
+            flat.all_gather()
+        torch.cuda.synchronize()
+        barrier()
+        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        a.record(stream)
+        for _ in range(nb):
+            flat.reduce_scatter_grads()
+        b.record(stream)
+        for _ in range(nb):
+            flat.reduce_scatter_grads()
+            opt.step()
+            flat.all_gather()
+        c.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / nb, b.elapsed_time(c) / nb], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        zero1["reduce_scatter_ms"] = float(t[0])
+        zero1["reduce_scatter_step_allgather_ms"] = float(t[1])
+        zero1["reduce_scatter_step_allgather_params_per_s"] = total_params / (float(t[1]) * 1e-3)
 
     # ---- e2e through the public API with host buffers (pinned): H2D grads, step, D2H params.
     # The owned tensors are split into chunks of about equal size, each with its

@@ -15,6 +15,13 @@ Two exchanges:
     in-place all-gather completes the step, with every link busy in both
     directions;
   * per tensor: an async broadcast of each tensor from its owner.
+
+With ``reduce_grads=True`` the gradients live in a second flat buffer of the
+same layout (``p.grad`` are views of it) and one reduce-scatter before the
+local step leaves every rank the summed (by default averaged) gradients of the
+tensors it owns: the communication pattern of ZeRO-2 (reduce-scatter of
+gradients, local step, all-gather of parameters) in place of a full
+all-reduce.
 """
 
 from __future__ import annotations
@@ -96,6 +103,7 @@ class FlatParams:
             fill[r] += (p.numel() + self.ALIGN - 1) // self.ALIGN * self.ALIGN
         self.shard = max(max(fill), self.ALIGN)
         self.buffer = torch.zeros(world * self.shard, dtype=dtype, device=dev)
+        self.grad_buffer = None
 
     def bind(self):
         with torch.no_grad():
@@ -107,6 +115,32 @@ class FlatParams:
 
     def local_slot(self):
         return self.buffer.narrow(0, self.rank * self.shard, self.shard)
+
+    def bind_grads(self):
+        """Gradients as views of one flat buffer of the parameter layout (existing
+        gradients are copied in); backward accumulates into the views."""
+        self.grad_buffer = torch.zeros_like(self.buffer)
+        with torch.no_grad():
+            for p, r, off in zip(self.params, self.owner, self.offsets):
+                view = self.grad_buffer.narrow(0, r * self.shard + off, p.numel()).view(p.shape)
+                if p.grad is not None:
+                    view.copy_(p.grad)
+                p.grad = view
+        return self
+
+    def reduce_scatter_grads(self, group=None, average: bool = True, async_op: bool = False):
+        """Sum every rank's gradients into the owner's slot, in place (this
+        rank's slot of the gradient buffer), divided by the world size when
+        ``average``; the other slots keep this rank's own gradients."""
+        slot = self.grad_buffer.narrow(0, self.rank * self.shard, self.shard)
+        work = dist.reduce_scatter_tensor(slot, self.grad_buffer, op=dist.ReduceOp.SUM, group=group,
+                                          async_op=async_op)
+        if average:
+            if work is not None:
+                work.wait()
+                work = None
+            slot.div_(self.world)
+        return work
 
     def all_gather(self, group=None, async_op: bool = False):
         """Every rank's slot to every rank, in place (input = this rank's slot)."""
@@ -131,7 +165,8 @@ class Zero1:
     or dtype.  ``flat=False`` always broadcasts per tensor.
     """
 
-    def __init__(self, params, optimizer_cls, process_group=None, flat: bool = True, **kwargs):
+    def __init__(self, params, optimizer_cls, process_group=None, flat: bool = True, reduce_grads: bool = False,
+                 average_grads: bool = True, **kwargs):
         self.group = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
@@ -144,6 +179,13 @@ class Zero1:
         self.flat = None
         if flat and self.world > 1 and len({(p.device, p.dtype) for p in self.params}) == 1:
             self.flat = FlatParams(self.params, self.owner, self.world, self.rank).bind()
+        self.reduce_grads = bool(reduce_grads)
+        self.average_grads = bool(average_grads)
+        if self.reduce_grads:
+            if self.world > 1 and self.flat is None:
+                raise ValueError("reduce_grads needs the flat layout (one device and dtype for every parameter)")
+            if self.flat is not None:
+                self.flat.bind_grads()
         self.owned = [p for p, r in zip(self.params, self.owner) if r == self.rank]
         self.optimizer = optimizer_cls(self.owned, **kwargs) if self.owned else None
 
@@ -180,11 +222,16 @@ class Zero1:
         if closure is not None:
             with torch.enable_grad():
                 loss = closure()
+        if self.reduce_grads and self.flat is not None:
+            self.flat.reduce_scatter_grads(self.group, average=self.average_grads)
         self.local_step()
         self.exchange_params()
         return loss
 
     def zero_grad(self, set_to_none: bool = True):
+        if self.reduce_grads and self.flat is not None:
+            self.flat.grad_buffer.zero_()  # the gradient views stay bound
+            return
         for p in self.params:
             if set_to_none:
                 p.grad = None

@@ -51,8 +51,8 @@ def _worker(rank, world, port, mode, out):
         params = [torch.nn.Parameter(t) for t in _params(0)]
         grads = _params(1)
         for p, g in zip(params, grads):
-            p.grad = g.clone()
-        z = zero.Zero1(params, StandIn, lr=0.5, flat=(mode != "bcast"))
+            p.grad = g.clone() * (rank + 1 if mode == "rs" else 1)
+        z = zero.Zero1(params, StandIn, lr=0.5, flat=(mode != "bcast"), reduce_grads=(mode == "rs"))
         if mode != "bcast":
             # every parameter is a 256-byte aligned view of the one flat buffer
             base = z.flat.buffer.data_ptr()
@@ -125,13 +125,15 @@ def test_step_bytes_formula():
     assert zero.step_bytes((1024, 1024), "SMO", k_ratio=0.5) == 12 * 1024 * 1024 + 16 * 512 * 512
 
 
-@pytest.mark.parametrize("mode", ["ok", "bcast"])
+@pytest.mark.parametrize("mode", ["ok", "bcast", "rs"])
 def test_zero1_exchange_makes_replicas_identical(mode):
     out, codes = _run(mode)
     assert codes == [0, 0]
     (s0, p0, own0), (s1, p1, own1) = out[0], out[1]
     assert s0 == s1 == "ok" and own0 == own1 and set(own0) == {0, 1}
-    expected = [p - 0.5 * g for p, g in zip(_params(0), _params(1))]
+    # "rs": rank r's gradients are (r + 1) g; the reduce-scatter averages them to 1.5 g
+    scale = 1.5 if mode == "rs" else 1.0
+    expected = [p - 0.5 * scale * g for p, g in zip(_params(0), _params(1))]
     for a, b, e in zip(p0, p1, expected):
         assert torch.equal(a, b)
         assert torch.allclose(a, e)
