@@ -59,6 +59,33 @@ def test_status_strings_and_host_side_validation():
     assert lib.smo_step(t.ctypes.data, 0, addr, 2048, None) == 0           # empty step is a no-op
 
 
+def test_permutation_descriptor_rules():
+    """permute_basis index arrays: all four or none, pooled kinds only, no bands."""
+    lib = _lib.load()
+    ws = (ctypes.c_uint8 * 4096)()
+    addr = (ctypes.addressof(ws) + 255) // 256 * 256
+    t = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    t["kind"] = _lib.SMO_KIND_POOLED8
+    t["rows"], t["cols"], t["comp_rows"], t["comp_cols"], t["q_block"] = 64, 64, 16, 16, 64
+    base = 1 << 32
+    for k in ("param", "grad", "m_q_in", "m_s_in", "v_q_in", "v_s_in", "m_q_out", "m_s_out", "v_q_out", "v_s_out"):
+        t[k] = base
+        base += 1 << 20
+    t["row_perm"] = base                                                     # one of four
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 1
+    t["col_perm"], t["row_perm_inv"], t["col_perm_inv"] = base + 1024, base + 2048, base + 3072
+    t["interp_band"] = 4                                                     # bands + permutation
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 1
+    t["interp_band"] = 0
+    t["col_perm"] = base + 1028                                              # misaligned int64 array
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 2
+    d = np.zeros(1, dtype=_lib.TENSOR_DTYPE)                                 # dense kind with a permutation
+    d["kind"], d["rows"], d["cols"] = _lib.SMO_KIND_DENSE, 16, 1
+    d["param"] = d["grad"] = d["m_in"] = d["v_in"] = d["m_out"] = d["v_out"] = 1 << 32
+    d["row_perm"] = d["col_perm"] = d["row_perm_inv"] = d["col_perm_inv"] = 1 << 33
+    assert lib.smo_step(d.ctypes.data, 1, addr, 2048, None) == 1
+
+
 @pytest.mark.parametrize("name", list(C.CASES))
 def test_host_rules_match_reference_metadata(name):
     """compression_view / comp_shape / q_block / quant_only layout agree with the
