@@ -324,6 +324,18 @@ __device__ __forceinline__ void phase1(const FusedDesc &d, int c, float2 *row, b
     else phase1_wd<KH, KW, CELLS, NT, false>(d, c, row, own);
 }
 
+// round(x / s * 127) with the dead-zone lift for a finite block scale
+// s <= 2^126 (then |x| <= s, the quotient is at most 1 and no clamp or
+// special case is needed); rs = RN(1/s)
+__device__ __forceinline__ int8_t quantize_finite(float x, float s, float rs) {
+    const float q0 = __fmul_rn(x, rs);
+    const float q = __fmaf_rn(__fmaf_rn(q0, -s, x), rs, q0);
+    float r = rintf(__fmul_rn(q, 127.0f));
+    const float lift = x != 0.0f ? copysignf(1.0f, x) : 0.0f;
+    r = r == 0.0f ? lift : r;
+    return (int8_t)__float2int_rn(r);
+}
+
 // Requantise the int8 blocks that compact row c completes.  A block spans at
 // most two compact rows (q_block <= w), both still in the ring.
 __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, int c, const float2 *Rc,
@@ -341,12 +353,18 @@ __device__ __forceinline__ void requant_block(const FusedDesc &d, uint32_t b, in
     }
     const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
     const float rm = __frcp_rn(sm), rv = __frcp_rn(sv);
+    const bool finite = sm <= 0x1p126f && sv <= 0x1p126f;  // uniform across the warp; false for NaN
     for (uint32_t k = lane; k < B; k += 32) {
         const uint32_t cell = b * B + k;
         float2 mv = f2(0.0f, 0.0f);
         if (cell < C) mv = (aligned || cell >= rowbase) ? Rc[cell - rowbase] : Rp[cell + w - rowbase];
-        d.mq_out[cell] = quantize_rc(mv.x, sm, rm);
-        d.vq_out[cell] = quantize_rc(mv.y, sv, rv);
+        if (finite) {
+            d.mq_out[cell] = quantize_finite(mv.x, sm, rm);
+            d.vq_out[cell] = quantize_finite(mv.y, sv, rv);
+        } else {
+            d.mq_out[cell] = quantize_rc(mv.x, sm, rm);
+            d.vq_out[cell] = quantize_rc(mv.y, sv, rv);
+        }
     }
     if (lane == 0) {
         d.ms_out[b] = sm;
