@@ -34,6 +34,7 @@
 // step later; that second read is meant to hit L2.
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "smo_common.cuh"
@@ -733,10 +734,23 @@ static int pick_threads(const FusedBatch &b) {
     return idle384 <= idle256 ? 384 : 256;
 }
 
+constexpr int kMaxDevices = 64;
+
+static int current_device() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -1;
+    return dev;
+}
+
+// SM count of the current device, queried once per device
 static int device_sm_count() {
-    int dev = 0, sms = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    static int cached[kMaxDevices];
+    const int dev = current_device();
+    if (dev < 0) return 148;
+    if (cached[dev] > 0) return cached[dev];
+    int sms = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) return 148;
+    cached[dev] = sms;
     return sms;
 }
 
@@ -821,11 +835,34 @@ static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, 
     const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
     const int nt = pick_threads(b);
     auto kern = fused_kernel_for<KH, KW>(nt);
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+    // The shared-memory attribute and the occupancy of this kernel instance
+    // are set and queried once per device and size (the attribute is a
+    // maximum, so a larger earlier setting covers smaller launches).
+    struct Cache {
+        size_t smem_attr = 0, smem_occ = 0;
+        int per_sm = 0;
+    };
+    static Cache cache[kMaxDevices][2];
+    static std::mutex mu;
+    const int dev = current_device();
     int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nt, smem);
-    if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        Cache scratch;
+        Cache &c = dev >= 0 ? cache[dev][nt == 384] : scratch;
+        cudaError_t e = cudaSuccess;
+        if (smem > c.smem_attr) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+            c.smem_attr = smem;
+        }
+        if (c.per_sm == 0 || c.smem_occ != smem) {
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c.per_sm, kern, nt, smem);
+            if (e != cudaSuccess) return (c.per_sm = 0, g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+            c.smem_occ = smem;
+        }
+        per_sm = c.per_sm;
+    }
     per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
     const int64_t strips = b.strip_start[b.n];
     int64_t grid = (int64_t)device_sm_count() * per_sm;
@@ -838,7 +875,7 @@ static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, 
     body += align_up(halo_floats * sizeof(float));
     float *heads = (float *)body;
     kern<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
-    e = cudaGetLastError();
+    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;
     return SMO_OK;

@@ -86,6 +86,7 @@ class _SpatialBase(Optimizer):
         self._workspace = {}    # device index -> uint8 workspace tensor
         self._hyper_cache = {}
         self._inv_perm = {}     # param -> (row_perm, col_perm, their inverses) for permute_basis
+        self._rows = {}         # param -> {row key: finished descriptor row (uint64 words)}
         # smo_tensor.flags for every tensor (SMO_FLAG_GENERAL_PATH pins the
         # general two-launch kernels; used to cross-check the fused kernel)
         self._kernel_flags = 0
@@ -96,14 +97,21 @@ class _SpatialBase(Optimizer):
         super().load_state_dict(state_dict)
         self._spare.clear()
         self._inv_perm.clear()
+        self._rows.clear()
 
     def _hyper(self, group, step):
+        return self._hyper_words(group, step)[0]
+
+    def _hyper_words(self, group, step):
+        """(smo_hyper tuple, the same 40 bytes as five uint64 words) of a group at a step."""
         betas = group["betas"]
         key = (group["lr"], betas[0], betas[1], group["eps"], group["weight_decay"], step)
         hp = self._hyper_cache.get(key)
         if hp is None:
             s = _host.step_scalars(group["lr"], betas, group["eps"], group["weight_decay"], step)
-            hp = (s.beta1, s.omb1, s.beta2, s.omb2, s.wd, s.wd_on, s.neg_step, s.sqrt_bc2, s.eps, 0)
+            tup = (s.beta1, s.omb1, s.beta2, s.omb2, s.wd, s.wd_on, s.neg_step, s.sqrt_bc2, s.eps, 0)
+            words = np.array([tup], dtype=_lib.HYPER_DTYPE).view(np.uint64).reshape(-1).copy()
+            hp = (tup, words)
             if len(self._hyper_cache) > 4096:
                 self._hyper_cache.clear()
             self._hyper_cache[key] = hp
@@ -152,14 +160,54 @@ class _SpatialBase(Optimizer):
     def _check_compress(self, group):
         pass
 
+    # Descriptor rows: the first time a tensor is seen with a given set of
+    # buffers, _fill writes its row field by field; the finished row is kept
+    # (keyed by the parameter's and the current moment buffer's addresses, the
+    # group and the kernel flags, so the two ping-pong parities get one row
+    # each) and later steps only patch the gradient address and the step's
+    # scalars.
+    _ROW_WORDS = _lib.TENSOR_DTYPE.itemsize // 8
+    _GRAD_WORD = _lib.TENSOR_DTYPE.fields["grad"][1] // 8
+    _HP_WORD = _lib.TENSOR_DTYPE.fields["hp"][1] // 8
+    _HP_WORDS = _lib.HYPER_DTYPE.itemsize // 8
+
+    @staticmethod
+    def _moment_ptr(state):
+        t = state.get("m_q")
+        if t is None:
+            t = state.get("exp_avg")
+        return t.data_ptr() if t is not None else 0
+
+    def _row(self, p, grad, state, group):
+        perm = state.get("row_perm")
+        key = (p.data_ptr(), self._moment_ptr(state), id(group), self._kernel_flags,
+               getattr(self, "low_peak", False), getattr(self, "band_mb", 0.0),
+               perm.data_ptr() if perm is not None else 0)
+        rows = self._rows.get(p)
+        if rows is None:
+            rows = self._rows[p] = {}
+        row = rows.get(key)
+        if row is None:
+            rec = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+            self._fill(rec[0], p, grad, state, group)
+            row = rec.view(np.uint64).reshape(-1).copy()
+            if len(rows) >= 4:
+                rows.clear()
+            rows[key] = row
+        return row
+
     def _launch(self, dev, items):
-        table = np.zeros(len(items), dtype=_lib.TENSOR_DTYPE)
+        words = np.empty((len(items), self._ROW_WORDS), dtype=np.uint64)
         keep = []
+        g0, h0, h1 = self._GRAD_WORD, self._HP_WORD, self._HP_WORD + self._HP_WORDS
         for i, (p, grad, state, group) in enumerate(items):
             if not grad.is_contiguous():
                 grad = grad.contiguous()
                 keep.append(grad)
-            self._fill(table[i], p, grad, state, group)
+            words[i] = self._row(p, grad, state, group)
+            words[i, g0] = grad.data_ptr()
+            words[i, h0:h1] = self._hyper_words(group, state["step"])[1]
+        table = words.view(_lib.TENSOR_DTYPE).reshape(-1)
         with torch.cuda.device(dev):
             nbytes = _lib.workspace_size(table)
             ws = self._workspace.get(dev.index)
