@@ -93,8 +93,21 @@ class _SpatialBase(Optimizer):
 
     # ---------------------------------------------------------------- state
 
+    # dtypes of the state tensors that are not the parameter's dtype
+    _STATE_DTYPES = (("m_q", torch.int8), ("v_q", torch.int8), ("m_s", torch.float32), ("v_s", torch.float32),
+                     ("row_perm", torch.int64), ("col_perm", torch.int64))
+
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)
+        # torch.optim.Optimizer.load_state_dict casts every state tensor of a
+        # floating-point parameter (except "step") to the parameter's dtype,
+        # which turns the int8 codes and int64 permutations into float
+        # tensors; the values are exact integers, so cast them back
+        for st in self.state.values():
+            for key, dtype in self._STATE_DTYPES:
+                t = st.get(key)
+                if torch.is_tensor(t) and t.dtype != dtype:
+                    st[key] = t.to(dtype).contiguous()
         self._spare.clear()
         self._inv_perm.clear()
         self._rows.clear()
@@ -363,6 +376,11 @@ class SMO8bit(_SpatialBase):
         return sp
 
     def _fill(self, rec, p, grad, state, group):
+        for key, dtype in self._STATE_DTYPES:
+            t = state.get(key)
+            if t is not None and (t.dtype != dtype or t.device != p.device or not t.is_contiguous()):
+                raise TypeError(f"state['{key}'] must be a contiguous {dtype} tensor on {p.device}; "
+                                f"got {t.dtype} on {t.device}")
         rec["param"] = p.data_ptr()
         rec["grad"] = grad.data_ptr()
         rec["flags"] = self._kernel_flags

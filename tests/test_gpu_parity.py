@@ -308,3 +308,58 @@ def test_fused_fp32_moments_4x4_vs_oracle():
     for key in ("exp_avg", "exp_avg_sq"):
         assert np.array_equal(host(st[key]).reshape(-1), np.asarray(rst[key]).reshape(-1)), key
     assert np.array_equal(host(p).view(np.uint32), ref_p.view(np.uint32))
+
+
+def test_state_dict_round_trip_continues_bit_identically():
+    """state_dict() / load_state_dict(): a run restored from a mid-run snapshot
+    (into the same optimizer, and into a fresh one) continues exactly as the
+    uninterrupted run, for pooled int8, dense and quant_only tensors."""
+    import copy
+    shapes = [(128, 512), (384, 1152), (300,), (64, 48)]
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01, k_ratio=0.25, block_size=64)
+
+    def make():
+        ps = [torch.nn.Parameter(cuda(synthetic.synth_param(30, i, s))) for i, s in enumerate(shapes)]
+        groups = [{"params": ps[:3]}, {"params": ps[3:], "compress": "quant_only"}]
+        return ps, SMO8bit(groups, **kw)
+
+    def run(ps, opt, steps):
+        for step in steps:
+            for i, (p, s) in enumerate(zip(ps, shapes)):
+                p.grad = cuda(synthetic.synth_grad(30, step, i, s))
+            opt.step()
+        torch.cuda.synchronize()
+
+    pa, oa = make()
+    run(pa, oa, (1, 2, 3))
+    snap_p = [p.detach().clone() for p in pa]
+    snap_s = copy.deepcopy(oa.state_dict())
+    run(pa, oa, (4, 5))
+    final = [p.detach().clone() for p in pa]
+
+    # the same optimizer, rewound
+    with torch.no_grad():
+        for p, s in zip(pa, snap_p):
+            p.copy_(s)
+    oa.load_state_dict(copy.deepcopy(snap_s))
+    run(pa, oa, (4, 5))
+    for i, (p, f) in enumerate(zip(pa, final)):
+        assert torch.equal(p, f), f"param {i} differs after rewinding the same optimizer"
+
+    # a fresh optimizer
+    pb, ob = make()
+    with torch.no_grad():
+        for p, s in zip(pb, snap_p):
+            p.copy_(s)
+    ob.load_state_dict(copy.deepcopy(snap_s))
+    run(pb, ob, (4, 5))
+    for i, (p, f) in enumerate(zip(pb, final)):
+        assert torch.equal(p, f), f"param {i} differs in a fresh optimizer"
+    sa, sb = oa.state_dict()["state"], ob.state_dict()["state"]
+    for k in sa:
+        for key, v in sa[k].items():
+            if torch.is_tensor(v):
+                assert torch.equal(v, sb[k][key]), f"state {k}.{key} differs"
+            else:
+                assert v == sb[k][key], f"state {k}.{key} differs"
+    assert oa.workspace_status() == 0 and ob.workspace_status() == 0
