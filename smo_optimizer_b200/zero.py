@@ -240,3 +240,8 @@ class Zero1:
 
     def state_dict(self):
         return self.optimizer.state_dict() if self.optimizer else {"state": {}, "param_groups": []}
+
+    def load_state_dict(self, state_dict):
+        """Load this rank's shard (what ``state_dict()`` returned on the same rank)."""
+        if self.optimizer is not None:
+            self.optimizer.load_state_dict(state_dict)
