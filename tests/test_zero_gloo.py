@@ -65,7 +65,15 @@ def _worker(rank, world, port, mode, out):
         t0 = time.time()
         try:
             z.step()
-            out[rank] = ("ok", [p.detach().clone() for p in params], z.owner)
+            result = [p.detach().clone() for p in params]
+            if mode == "rs":
+                # zero_grad keeps every gradient a view of the flat buffer, zeroed
+                z.zero_grad()
+                base = z.flat.grad_buffer.data_ptr()
+                end = base + z.flat.grad_buffer.numel() * 4
+                assert all(p.grad is not None and base <= p.grad.data_ptr() < end for p in params)
+                assert float(z.flat.grad_buffer.abs().sum()) == 0.0
+            out[rank] = ("ok", result, z.owner)
         except Exception as e:  # the peer is gone: the collective must fail, not hang
             out[rank] = ("error", type(e).__name__, time.time() - t0)
     finally:
