@@ -363,3 +363,56 @@ def test_state_dict_round_trip_continues_bit_identically():
             else:
                 assert v == sb[k][key], f"state {k}.{key} differs"
     assert oa.workspace_status() == 0 and ob.workspace_status() == 0
+
+
+@pytest.mark.parametrize("seed", [101, 102, 103, 104])
+def test_random_mixed_sets_bit_exact_vs_oracle(seed):
+    """One step call over a random mix of tensor kinds and shapes: exact and
+    adaptive pooled windows (fused and general kernels), row-straddling blocks,
+    dense 1-D and small tensors, a quant_only group; monolithic or low_peak, or
+    permute_basis; bit-identical to the oracle after three steps."""
+    rng = np.random.default_rng(seed)
+    shapes = []
+    for _ in range(6):
+        h = int(rng.integers(9, 80)) * (4 if rng.random() < 0.6 else 1) + (0 if rng.random() < 0.7 else 3)
+        w = int(rng.integers(9, 180)) * (4 if rng.random() < 0.6 else 1)
+        shapes.append((max(h, 33), max(w, 33)))
+    shapes += [(int(rng.integers(20, 500)),), (16, 24)]
+    quant_shapes = [(int(rng.integers(40, 120)), int(rng.integers(40, 120))), (int(rng.integers(50, 900)),)]
+    mode = ("mono", "band", "perm", "mono")[seed % 4]
+    kw = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.01 if seed % 2 else 0.0, k_ratio=0.25,
+              block_size=int(rng.choice([32, 64, 100])))
+    if mode == "band":
+        kw.update(low_peak=True, band_mb=0.05)
+    if mode == "perm":
+        kw.update(permute_basis=True)
+    all_shapes = shapes + quant_shapes
+    p0 = [synthetic.synth_param(seed, i, s) for i, s in enumerate(all_shapes)]
+    ps = [torch.nn.Parameter(cuda(a)) for a in p0]
+    opt = SMO8bit([{"params": ps[:len(shapes)]}, {"params": ps[len(shapes):], "compress": "quant_only"}], **kw)
+    ref_p = [a.copy() for a in p0]
+    ref = oracle.OracleOptimizer("SMO8bit", [{"params": ref_p[:len(shapes)]},
+                                             {"params": ref_p[len(shapes):], "compress": "quant_only"}], **kw)
+    keys = [k for k, _, _ in ref.params()]
+    for step in range(1, 4):
+        gs = [synthetic.synth_grad(seed, step, i, s) for i, s in enumerate(all_shapes)]
+        for p, g in zip(ps, gs):
+            p.grad = cuda(g)
+        opt.step()
+        if step == 1 and mode == "perm":
+            # the oracle takes the permutations the library drew at its first step
+            for p, k in zip(ps, keys):
+                st = opt.state[p]
+                if "row_perm" in st:
+                    ref.preset_perms[k] = (host(st["row_perm"]), host(st["col_perm"]))
+        ref.step(gs)
+    torch.cuda.synchronize()
+    assert opt.workspace_status() == 0
+    for i, (p, k) in enumerate(zip(ps, keys)):
+        st, rst = opt.state[p], ref.state[k]
+        for key in C.STATE_ARRAY_KEYS:
+            if key in rst:
+                assert np.array_equal(host(st[key]).reshape(-1), np.asarray(rst[key]).reshape(-1)), \
+                    f"tensor {i} {all_shapes[i]} state {key}"
+        assert np.array_equal(host(p).view(np.uint32).reshape(-1), ref_p[i].view(np.uint32).reshape(-1)), \
+            f"tensor {i} {all_shapes[i]} param"
