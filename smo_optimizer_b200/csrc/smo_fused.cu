@@ -108,19 +108,20 @@ __device__ __forceinline__ void load_grad_row(const float *ptr, float (&v)[KW]) 
     }
 }
 
-// parameter loads: L2-cached (phase 1, re-read one pipeline step later) or last use (phase 2)
+// parameter loads: cached (phase 1: the next cell was prefetched into L1, and
+// the row is re-read from L2 one pipeline step later) or last use (phase 2)
 template <int KW, bool kLastUse>
 __device__ __forceinline__ void load_param_row(const float *ptr, float (&v)[KW]) {
     if constexpr (KW % 4 == 0) {
 #pragma unroll
         for (int k = 0; k < KW / 4; k++) {
             const float4 *q = reinterpret_cast<const float4 *>(ptr) + k;
-            float4 t = kLastUse ? __ldlu(q) : __ldcg(q);
+            float4 t = kLastUse ? __ldlu(q) : __ldca(q);
             v[4 * k] = t.x; v[4 * k + 1] = t.y; v[4 * k + 2] = t.z; v[4 * k + 3] = t.w;
         }
     } else {
         const float2 *q = reinterpret_cast<const float2 *>(ptr);
-        float2 t = kLastUse ? __ldlu(q) : __ldcg(q);
+        float2 t = kLastUse ? __ldlu(q) : __ldca(q);
         v[0] = t.x; v[1] = t.y;
     }
 }
@@ -308,6 +309,18 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
                 if (WD) {
 #pragma unroll
                     for (int i = 0; i < KH; i++) load_param_row<KW, false>(pb + i * W + (int64_t)j * KW, pv[u][i]);
+                }
+            }
+        }
+        {
+            // while this cell is summed, pull the thread's next cell of the row
+            // into L1 (one lane of eight covers a 128-byte line)
+            const int jn = j0 + CELLS * NT;
+            if (jn < w && (threadIdx.x & 7) == 0) {
+#pragma unroll
+                for (int i = 0; i < KH; i++) {
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(gb + i * W + (int64_t)jn * KW));
+                    if (WD) asm volatile("prefetch.global.L1 [%0];" ::"l"(pb + i * W + (int64_t)jn * KW));
                 }
             }
         }
