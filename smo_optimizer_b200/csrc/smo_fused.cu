@@ -403,17 +403,38 @@ struct RowCo {
 };
 
 // Row weights of the KH output rows of compact row c (threads 0..KH-1).
+// This is row_coef (smo_common.cuh) specialised to exact KH-row windows:
+// output row c*KH + i lies in compact row c, so the band of a low_peak tensor
+// is (c / band) * band without 64-bit divisions, and the interpolation scale
+// n / (n*KH) of a band (or h / H of the whole tensor) is exactly 1/KH because
+// fused_takes keeps H below 2^24, where both operands are exact floats.  The
+// remaining float operations are row_coef's, in its order.
 template <int KH>
 __device__ __forceinline__ void compute_rowco(const FusedDesc &d, int c, RowCo *dst) {
     if (threadIdx.x < KH) {
-        int small;
-        const Coef rc = row_coef((int64_t)c * KH + threadIdx.x, d.H, d.h, d.W, d.band, small);
+        const int i = threadIdx.x;
+        int a = 0, n = d.h;  // rows [a, a + n) are interpolated together
+        if (d.band > 0) {
+            const int band = (int)d.band;
+            const int s0 = (c / band) * band;
+            const int s1 = s0 + band < d.h ? s0 + band : d.h;
+            a = s0 > 0 ? s0 - 1 : 0;
+            n = (s1 + 1 < d.h ? s1 + 1 : d.h) - a;
+        }
+        const int o = (c - a) * KH + i;  // output row in the band's coordinates
+        float real = __fmaf_rn(1.0f / KH, __fadd_rn((float)o, 0.5f), -0.5f);
+        real = real < 0.0f ? 0.0f : real;
+        int i0 = (int)floorf(real);
+        i0 = i0 > n - 1 ? n - 1 : i0;
+        float l1 = __fsub_rn(real, (float)i0);
+        l1 = l1 < 0.0f ? 0.0f : (l1 > 1.0f ? 1.0f : l1);
+        const int i1 = i0 + (i0 < n - 1 ? 1 : 0);
         RowCo r;
-        r.s0 = (int)(rc.i0 - (c - 1));
-        r.s1 = (int)(rc.i1 - (c - 1));
-        r.l0 = rc.l0;
-        r.l1 = rc.l1;
-        dst[threadIdx.x] = r;
+        r.s0 = i0 + a - (c - 1);
+        r.s1 = i1 + a - (c - 1);
+        r.l0 = __fsub_rn(1.0f, l1);
+        r.l1 = l1;
+        dst[i] = r;
     }
 }
 
@@ -702,6 +723,7 @@ bool fused_takes(const smo_tensor &t) {
     if (t.cols <= 128) return false;  // torch's small-output interpolation order
     if (t.comp_cols > kMaxFusedCols) return false;
     if (t.comp_rows * t.comp_cols >= ((int64_t)1 << 31)) return false;  // 32-bit cell indices
+    if (t.rows >= ((int64_t)1 << 24)) return false;  // exact float row coordinates (compute_rowco)
     if (t.kind == SMO_KIND_POOLED8 && t.q_block > t.comp_cols) return false;
     const size_t a = kw % 4 == 0 ? 16 : 8;
     if ((uintptr_t)t.param % a || (uintptr_t)t.grad % a) return false;
