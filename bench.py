@@ -11,9 +11,11 @@ the tensors are sharded ZeRO-1 style: each rank steps the tensors it owns, and
 all-gather of the flat parameter buffer that completes a ZeRO-1 step is timed
 separately (``zero1``).  Rank 0 prints one JSON line.
 
-``--impl reference`` times the CPU restatement of the reference step (the
-oracle, all host threads) on the same workload, one tensor per step in
-round-robin order, and prints the same metric.
+``--impl reference`` times the reference's own CPU step (its PyTorch
+SMO8bit / SMO, installed unmodified in baseline/_ref) on all host cores over
+the same workload: whole-set steps when K + W of them fit about two minutes,
+else round-robin samples of the set; without baseline/_ref it times the C
+restatement of the step (the oracle) the same way.  Same metric and config.
 """
 
 from __future__ import annotations
@@ -141,14 +143,21 @@ def build_workload(wl, seed, device, owned):
     return params, grads
 
 
+def _all_host_threads():
+    """Every host core: torch.distributed.run sets OMP_NUM_THREADS=1 for its
+    ranks, which the CPU legs override."""
+    return max(1, os.cpu_count() or 1)
+
+
 def cpu_baseline(wl, seed, seconds):
-    """The oracle (CPU restatement of the reference step) on a sample of the workload."""
+    """The oracle (C restatement of the reference step, OpenMP) on a sample of the workload."""
     import numpy as np
 
     from oracle import oracle
-    from smo_optimizer_b200 import synthetic, zero
+    from smo_optimizer_b200 import synthetic
 
     oracle.build()
+    oracle.set_num_threads(_all_host_threads())
     # one decoder layer's tensors (or the first few of another workload)
     take = []
     total = 0
@@ -173,55 +182,210 @@ def cpu_baseline(wl, seed, seconds):
                       f"{el:.1f} s, OpenMP C oracle"}
 
 
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def import_reference():
+    """The reference's own optimizer classes, installed unmodified into
+    baseline/_ref (``pip install --target baseline/_ref``); None when absent."""
+    if not os.path.isdir(os.path.join(REF_DIR, "smo")):
+        return None, "reference not installed in baseline/_ref"
+    if REF_DIR not in sys.path:
+        sys.path.insert(0, REF_DIR)
+    try:
+        from smo.optimizers.spatial import SMO as RefSMO
+        from smo.optimizers.spatial_8bit import SMO8bit as RefSMO8bit
+    except Exception as e:  # pragma: no cover - depends on the install
+        return None, f"reference import failed: {e!r}"
+    import smo
+    if not os.path.abspath(smo.__file__).startswith(REF_DIR):
+        return None, f"an smo package outside baseline/_ref shadows the reference ({smo.__file__})"
+    return {"SMO8bit": RefSMO8bit, "SMO": RefSMO}, None
+
+
+class ReferenceLeg:
+    """The reference's PyTorch step (SMO8bit / SMO from baseline/_ref) on the
+    host cores over the workload's tensors, timed as
+    benchmarks/suites/optimizer_step/benchmark_step_time.py:22-38 times it
+    (warm-up, then time.perf_counter around optimizer.step()).
+
+    Inputs are seeded torch CPU draws with the workload's shapes and
+    distributions (params N(0, 0.02), grads N(0, 1e-3), bf16-rounded where the
+    workload says so).  ``step(members)`` steps the tensors listed: one
+    optimizer per tensor, so that a bounded sample of the set can be timed when
+    the whole set does not fit the time budget."""
+
+    def __init__(self, wl, seed, classes):
+        import torch
+
+        from smo_optimizer_b200 import protected_param_groups
+
+        torch.set_num_threads(_all_host_threads())
+        self.torch = torch
+        self.wl = wl
+        gen = torch.Generator().manual_seed(seed)
+        cls = classes[wl.optimizer]
+        self.params, self.opts = [], []
+        flags = {}
+        if wl.protect_output:
+            # the reference harness's grouping rule (t4_memory_benchmark.py:117-133)
+            named = [(n, i) for i, (n, _) in enumerate(wl.tensors)]
+            for g in protected_param_groups(named, wl.protect_output, quant_capable=wl.optimizer == "SMO8bit"):
+                for i in g["params"]:
+                    flags[i] = g.get("compress", True)
+        for i, (_, shape) in enumerate(wl.tensors):
+            p = torch.nn.Parameter(torch.randn(shape, generator=gen) * 0.02)
+            g = torch.randn(shape, generator=gen) * 1e-3
+            if wl.bf16_grads:
+                g = g.to(torch.bfloat16).to(torch.float32)
+            p.grad = g
+            group = {"params": [p]}
+            if i in flags:
+                group["compress"] = flags[i]
+            self.params.append(p)
+            self.opts.append(cls([group], **wl.kwargs))
+        self.numel = [p.numel() for p in self.params]
+
+    def step(self, members):
+        t0 = time.perf_counter()
+        for i in members:
+            self.opts[i].step()
+        return time.perf_counter() - t0
+
+    def cores(self):
+        return self.torch.get_num_threads()
+
+
+def reference_baseline(wl, seed, seconds):
+    """cpu_baseline of kind "reference": the reference's own step on a sample
+    of the workload (about ``seconds`` of host time), or None if the reference
+    is not installed."""
+    classes, why = import_reference()
+    if classes is None:
+        return None
+    # about 25M params (the sample of the port leg)
+    take, total = [], 0
+    for i, (_, shape) in enumerate(wl.tensors):
+        take.append(i)
+        total += _numel(shape)
+        if total >= 25_000_000:
+            break
+    sub = type(wl)(wl.name, tuple(wl.tensors[i] for i in take), wl.optimizer, wl.kwargs, wl.protect_output,
+                   wl.bf16_grads)
+    leg = ReferenceLeg(sub, seed, classes)
+    members = list(range(len(take)))
+    leg.step(members)  # state init
+    steps, el = 0, 0.0
+    while el < seconds and steps < 1000:
+        el += leg.step(members)
+        steps += 1
+    return {"value": total * steps / el, "unit": UNIT, "cores": leg.cores(), "kind": "reference",
+            "sample": f"{len(take)} tensors ({total / 1e6:.1f}M params) of {wl.name}, {steps} steps, {el:.1f} s, "
+                      f"the reference's PyTorch {wl.optimizer}.step (baseline/_ref) on the host cores"}
+
+
+def _numel(shape):
+    n = 1
+    for s in shape:
+        n *= int(s)
+    return n
+
+
 def run_reference(args, rank, world):
-    """CPU restatement of the reference step (the oracle) on the host cores."""
+    """The reference arm: the reference's own CPU step (its PyTorch SMO8bit /
+    SMO, installed unmodified in baseline/_ref) on the host cores, on the
+    workload of the GPU arm.  Only rank 0 works; other ranks exit at once.
+
+    A step is one optimizer step over the whole parameter set when K + W such
+    steps fit the time budget (about two minutes), else over a round-robin
+    sample of the tensors sized to fit it.  Without baseline/_ref the C
+    restatement of the step (the oracle) is timed the same way."""
     if rank != 0:
         return 0
-    import numpy as np
+    from smo_optimizer_b200 import workloads
 
-    from oracle import oracle
-    from smo_optimizer_b200 import synthetic, workloads
-
-    oracle.build()
     wl = workloads.WORKLOADS[args.workload]
     n = len(wl.tensors)
-    # every tensor gets its own oracle optimizer so one step can touch one tensor
-    cache = {}
+    classes, why = import_reference()
+    budget = float(os.environ.get("SMO_REFERENCE_BUDGET_S", "120"))
+    if classes is not None:
+        leg = ReferenceLeg(wl, args.seed, classes)
+        kind = "reference"
+        what = f"the reference's PyTorch {wl.optimizer}.step (baseline/_ref)"
+        step_fn, cores = leg.step, leg.cores
+        numel = leg.numel
+    else:
+        from oracle import oracle
+        from smo_optimizer_b200 import synthetic
 
-    def tensor_opt(i):
-        if i not in cache:
-            shape = wl.tensors[i][1]
+        oracle.build()
+        oracle.set_num_threads(_all_host_threads())
+        opts = []
+        for i, (_, shape) in enumerate(wl.tensors):
             p = synthetic.synth_param(args.seed, i, shape)
             g = synthetic.synth_grad(args.seed, 1, i, shape, bf16=wl.bf16_grads)
-            o = oracle.OracleOptimizer(wl.optimizer, [{"params": [p]}], **wl.kwargs)
-            o.step([g])  # lazy state init outside the timed region
-            cache.clear()
-            cache[i] = (o, g, int(np.prod(shape)))
-        return cache[i]
+            opts.append((oracle.OracleOptimizer(wl.optimizer, [{"params": [p]}], **wl.kwargs), g))
 
+        def step_fn(members):
+            t0 = time.perf_counter()
+            for i in members:
+                opts[i][0].step([opts[i][1]])
+            return time.perf_counter() - t0
+
+        kind = "port"
+        what = f"the C restatement of the step (OpenMP oracle; {why})"
+        cores = oracle.num_threads
+        numel = [_numel(s) for _, s in wl.tensors]
+
+    full = list(range(n))
+    t_full = step_fn(full)  # state init + first step over the whole set
+    t_full = min(t_full, step_fn(full))
+    per_step = budget / max(1, args.steps + args.warmup)
+    if t_full <= per_step:
+        chunks = [full]
+        sample = f"whole set ({sum(numel) / 1e6:.1f}M params, {n} tensors) per step"
+    else:
+        # contiguous round-robin chunks of tensors, each about per_step long
+        frac = per_step / t_full
+        target = max(1, int(sum(numel) * frac))
+        chunks, cur, acc = [], [], 0
+        for i in full:
+            cur.append(i)
+            acc += numel[i]
+            if acc >= target:
+                chunks.append(cur)
+                cur, acc = [], 0
+        if cur:
+            chunks.append(cur)
+        sample = f"round-robin chunks of ~{target / 1e6:.0f}M params of the {sum(numel) / 1e6:.1f}M-param set per step"
     for w in range(args.warmup):
-        o, g, _ = tensor_opt(w % n)
-        o.step([g])
+        step_fn(chunks[w % len(chunks)])
     stepped, el = 0, 0.0
     for k in range(args.steps):
-        o, g, numel = tensor_opt((args.warmup + k) % n)
-        t0 = time.perf_counter()
-        o.step([g])
-        el += time.perf_counter() - t0
-        stepped += numel
+        c = chunks[(args.warmup + k) % len(chunks)]
+        el += step_fn(c)
+        stepped += sum(numel[i] for i in c)
     value = stepped / el
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * el / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32+int8",
-        "data": "synthetic",
-        "config": {"workload": wl.name, "params": wl.numel, "tensors": n, **_cfg(wl)},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-                         "sample": f"one tensor of {wl.name} per step, round robin ({stepped / 1e6:.0f}M params)"},
+        "data": "synthetic (seeded host draws, params N(0,0.02), grads N(0,1e-3))",
+        "config": _config(wl, world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores(), "kind": kind,
+                         "sample": f"{sample}; {what}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _config(wl, world):
+    gb = 8 * wl.numel / 1e9  # fp32 params and grads
+    l2 = (f"inputs ({gb:.1f} GB of params and grads) larger than L2; no flush" if gb > 0.5 else
+          f"inputs ({gb * 1e3:.0f} MB) fit in L2: a step re-reads what the previous step left there")
+    return {"workload": wl.name, "params": wl.numel, "tensors": len(wl.tensors),
+            "parallelism": f"zero1-dp{world}" if world > 1 else "single", **_cfg(wl), "l2": l2}
 
 
 def _cfg(wl):
@@ -469,22 +633,22 @@ def main():
                "path": "SMO8bit.step() via the C ABI, one optimizer per chunk of tensors; pinned host grads "
                        "H2D, step and params D2H pipelined over chunks on three streams"}
 
-    cpu = None
+    cpu = cpu_ref = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(wl, args.seed, args.cpu_sample_seconds)
+        cpu_ref = reference_baseline(wl, args.seed, args.cpu_sample_seconds)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32+int8", "data": "synthetic (seeded counter-hash N(0,0.02) params, N(0,1e-3) grads)",
-            "config": {"workload": wl.name, "params": total_params, "tensors": len(wl.tensors),
-                       "parallelism": f"zero1-dp{world}" if world > 1 else "single", **_cfg(wl),
-                       "l2": "inputs (>= 6 GB) larger than L2; no flush"},
+            "config": _config(wl, world),
             "hbm_gbs": sum(costs) / (ms_per_step * 1e-3) / 1e9,
             "kernel_ms_per_step": step_ms,
             "roofline": roof,
-            "cpu_baseline": cpu,
+            "cpu_baseline": cpu_ref or cpu,
+            "cpu_baseline_port": cpu,
             "e2e": e2e,
             "gpu_launches": int(launches),
             "clocks": clk,

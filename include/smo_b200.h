@@ -121,9 +121,21 @@ SMO_API size_t smo_workspace_size(const smo_tensor *tensors, int32_t n);
  * two steps that share a workspace must not overlap on the device. */
 SMO_API int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t workspace_bytes, void *stream);
 
-/* Device-side status of the last step that used `workspace` (waits for the
- * stream).  SMO_OK or SMO_ERR_TIMEOUT. */
+/* Device-side status of the steps that used `workspace` since the last call
+ * (waits for the stream): SMO_OK or SMO_ERR_TIMEOUT.  The status is sticky
+ * until read: a non-zero status is cleared by this call, so the next step
+ * starts clean.  No counterpart in the reference (its step is synchronous
+ * Python and raises directly). */
 SMO_API int smo_workspace_status(void *workspace, void *stream);
+
+/* Poll limit of the fused kernel's bounded inter-CTA waits for launches made
+ * after this call, process-wide; a negative value restores the default
+ * (2^22 polls).  Returns the previous setting (-1 = default).  A limit that
+ * runs out makes the step report SMO_ERR_TIMEOUT through
+ * smo_workspace_status() instead of waiting longer; the step's parameters are
+ * then not valid.  Diagnostic hook for exercising the failure path without a
+ * GPU fault.  No counterpart in the reference. */
+SMO_API int64_t smo_set_wait_limit(int64_t max_polls);
 
 /* Bytes of the fixed scratch array behind smo_step_no_alloc(). */
 #define SMO_NO_ALLOC_SCRATCH_BYTES ((size_t)32 << 20)
@@ -134,11 +146,14 @@ SMO_API int smo_workspace_status(void *workspace, void *stream);
  * counterpart in the reference.
  * Scratch comes from a 32 MiB array in the library's own device memory, held
  * on every GPU where the library's device code is loaded until the process
- * exits; the call allocates nothing.  A step whose smo_workspace_size() exceeds
- * SMO_NO_ALLOC_SCRATCH_BYTES is rejected with SMO_ERR_WORKSPACE before any work
- * is enqueued.  The first call on a device resolves that device's copy of the
- * array (cudaGetSymbolAddress, with the device current); make that first call
- * before any stream capture.  All calls share the one array and it keeps the
+ * exits; the call allocates nothing.  Descriptors are validated first (a bad
+ * one returns its error and touches nothing); then a step whose
+ * smo_workspace_size() exceeds SMO_NO_ALLOC_SCRATCH_BYTES is rejected with
+ * SMO_ERR_WORKSPACE before any work is enqueued.  The first call on a device
+ * resolves that device's copy of the array (cudaGetSymbolAddress, with the
+ * device current) and keeps the address for the life of the process; make
+ * that first call before any stream capture, and do not call this entry point
+ * on a device after cudaDeviceReset().  All calls share the one array and it keeps the
  * previous call's contents: calls that overlap on the GPU (other streams,
  * other threads) race and must be serialised by the caller.  If
  * device_status is not NULL (a device int32), the step's device-side status

@@ -435,6 +435,16 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
     }
 }
 
+int validate_tensors(const smo_tensor *t, int32_t n) {
+    if (n < 0 || (n > 0 && !t)) return SMO_ERR_INVALID;
+    for (int32_t i = 0; i < n; i++) {
+        DevDesc d;
+        const int st = make_desc(t[i], d);
+        if (st != SMO_OK) return st;
+    }
+    return SMO_OK;
+}
+
 static inline int64_t items_a(const DevDesc &d) {
     switch (d.kind) {
         case SMO_KIND_POOLED8: return (d.h * d.w + d.B - 1) / d.B;
@@ -495,9 +505,9 @@ size_t smo_workspace_size(const smo_tensor *tensors, int32_t n) {
     if (!tensors || n <= 0) return 0;
     size_t general = 0;
     for (int32_t i = 0; i < n; i++) general += general_scratch(tensors[i]);
-    size_t fused = fused_workspace_size(tensors, n);
-    size_t body = general > fused ? general : fused;
-    return body ? kWsHeader + body : kWsHeader;
+    const FusedLayout fl = fused_workspace_layout(tensors, n);
+    const size_t body = general > fl.body_bytes ? general : fl.body_bytes;
+    return kWsHeader + fl.flag_bytes + body;
 }
 
 int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t workspace_bytes, void *stream_ptr) {
@@ -506,22 +516,22 @@ int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t works
     cudaStream_t stream = (cudaStream_t)stream_ptr;
 
     // Validate everything before any launch: a bad descriptor launches nothing.
-    static thread_local Batch batch;
-    for (int32_t i = 0; i < n; i++) {
-        DevDesc d;
-        int st = make_desc(tensors[i], d);
-        if (st != SMO_OK) return st;
-    }
+    int st = validate_tensors(tensors, n);
+    if (st != SMO_OK) return st;
     const size_t need = smo_workspace_size(tensors, n);
     if (!workspace || workspace_bytes < need || !aligned(workspace, kScratchAlign)) return SMO_ERR_WORKSPACE;
     char *ws = (char *)workspace;
+    const size_t flag_bytes = fused_workspace_layout(tensors, n).flag_bytes;
 
     // Tensors the fused single-pass kernel takes (exact-window pooled shapes).
-    int st = fused_step(tensors, n, ws, workspace_bytes, stream);
+    st = fused_step(tensors, n, ws, flag_bytes, stream);
     if (st != SMO_OK) return st;
 
-    // Everything else goes through the general two-launch path, batched.
-    size_t off = kWsHeader;
+    // Everything else goes through the general two-launch path, batched; its
+    // scratch starts after the fused kernel's flag words.
+    static thread_local Batch batch;
+    const size_t base = kWsHeader + flag_bytes;
+    size_t off = base;
     batch.n = 0;
     for (int32_t i = 0; i < n; i++) {
         if (fused_takes(tensors[i])) continue;
@@ -538,20 +548,30 @@ int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t works
             st = launch_general(batch, stream);
             if (st != SMO_OK) return st;
             batch.n = 0;
-            off = kWsHeader;  // stream order: the next launch pair starts after this one ends
+            off = base;  // stream order: the next launch pair starts after this one ends
         }
     }
     if (batch.n > 0) return launch_general(batch, stream);
     return SMO_OK;
 }
 
+int64_t smo_set_wait_limit(int64_t max_polls) { return set_wait_limit(max_polls); }
+
 int smo_workspace_status(void *workspace, void *stream_ptr) {
     if (!workspace) return SMO_ERR_WORKSPACE;
+    cudaStream_t stream = (cudaStream_t)stream_ptr;
     WsHeader h;
-    cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)stream_ptr);
+    cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, stream);
     if (e != cudaSuccess) return cuda_fail(e);
-    e = cudaStreamSynchronize((cudaStream_t)stream_ptr);
+    e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return cuda_fail(e);
+    if (h.error) {
+        // read and cleared: the next step starts with a clean error word
+        WsHeader *d = (WsHeader *)workspace;
+        e = cudaMemsetAsync(&d->error, 0, 2 * sizeof(unsigned int), stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e);
+    }
     return h.error ? (int)h.error : SMO_OK;
 }
 

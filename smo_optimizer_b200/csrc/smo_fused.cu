@@ -32,6 +32,7 @@
 //
 // The parameter rows read in phase 1 are read again in phase 2 one pipeline
 // step later; that second read is meant to hit L2.
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -47,6 +48,16 @@ constexpr int kMaxFused = 104;
 constexpr int64_t kStripRows = 16;          // longest strip (compact rows); shorter when a launch has few
 constexpr int64_t kMaxFusedCols = 8192;     // compact columns (shared memory: 24 B per column)
 constexpr int64_t kDefaultWaitIters = 1 << 22;
+
+// Poll limit of the inter-CTA waits (smo_set_wait_limit; negative = default)
+static std::atomic<int64_t> g_wait_limit{-1};
+
+int64_t wait_limit() {
+    const int64_t v = g_wait_limit.load(std::memory_order_relaxed);
+    return v < 0 ? kDefaultWaitIters : v;
+}
+
+int64_t set_wait_limit(int64_t polls) { return g_wait_limit.exchange(polls < 0 ? -1 : polls); }
 
 // n / d for 32-bit unsigned n by a divisor fixed per tensor: multiply by a
 // precomputed magic number (Granlund-Montgomery / Hacker's Delight 10-1,
@@ -832,11 +843,14 @@ static void plan_launches(const smo_tensor *t, int32_t n, std::vector<LaunchGrou
 
 // Workspace after the header: [flags: one word per strip][published rows:
 // 2*w floats per strip][head rows: 4*max_w floats per CTA].  Sized for the
-// whole set; each window-group launch reuses the space.
-size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
+// whole set; each window-group launch reuses the space.  The flag words sit
+// in a region of their own that nothing else writes (the general path's
+// scratch starts after it): a flag word may only ever hold a launch epoch,
+// or a stale float could read as "strip published".
+FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n) {
     std::vector<LaunchGroup> groups;
     plan_launches(t, n, groups);
-    size_t need = 0;
+    FusedLayout out{0, 0};
     const size_t ctas = (size_t)device_sm_count() * kMaxFusedCtasPerSm;
     for (const LaunchGroup &g : groups) {
         size_t strips = 0, halo_floats = 0;
@@ -847,11 +861,12 @@ size_t fused_workspace_size(const smo_tensor *t, int32_t n) {
             halo_floats += (size_t)s * 2 * (size_t)t[k].comp_cols;
             max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
         }
-        const size_t bytes = align_up(strips * sizeof(unsigned int)) + align_up(halo_floats * sizeof(float)) +
-                             ctas * 4 * (size_t)max_w * sizeof(float);
-        need = need > bytes ? need : bytes;
+        const size_t flags = align_up(strips * sizeof(unsigned int));
+        const size_t body = align_up(halo_floats * sizeof(float)) + ctas * 4 * (size_t)max_w * sizeof(float);
+        out.flag_bytes = out.flag_bytes > flags ? out.flag_bytes : flags;
+        out.body_bytes = out.body_bytes > body ? out.body_bytes : body;
     }
-    return need;
+    return out;
 }
 
 // The kernel instance of a window shape and CTA width: 16-element windows take
@@ -866,7 +881,8 @@ static auto fused_kernel_for(int nt) {
 }
 
 template <int KH, int KW>
-static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
+static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, size_t flag_bytes,
+                              cudaStream_t stream) {
     const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
     const int nt = pick_threads(b);
     auto kern = fused_kernel_for<KH, KW>(nt);
@@ -903,23 +919,23 @@ static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, 
     int64_t grid = (int64_t)device_sm_count() * per_sm;
     grid = grid < strips ? grid : strips;
     WsHeader *hdr = (WsHeader *)ws;
-    char *body = ws + kWsHeader;
-    unsigned int *flags = (unsigned int *)body;
-    body += align_up((size_t)strips * sizeof(unsigned int));
+    unsigned int *flags = (unsigned int *)(ws + kWsHeader);
+    char *body = ws + kWsHeader + flag_bytes;
     float *halo = (float *)body;
     body += align_up(halo_floats * sizeof(float));
     float *heads = (float *)body;
-    kern<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, kDefaultWaitIters);
+    kern<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, wait_limit());
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;
     return SMO_OK;
 }
 
-static int dispatch(int key, FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, cudaStream_t stream) {
+static int dispatch(int key, FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, size_t flag_bytes,
+                    cudaStream_t stream) {
     switch (key) {
 #define SMO_FUSED_CASE(KH, KW) \
-    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, halo_floats, ws, stream);
+    case KH * 16 + KW: return launch_fused_group<KH, KW>(b, max_w, halo_floats, ws, flag_bytes, stream);
         SMO_FUSED_CASE(2, 2) SMO_FUSED_CASE(2, 4) SMO_FUSED_CASE(2, 8)
         SMO_FUSED_CASE(4, 2) SMO_FUSED_CASE(4, 4) SMO_FUSED_CASE(4, 8)
         SMO_FUSED_CASE(8, 2) SMO_FUSED_CASE(8, 4) SMO_FUSED_CASE(8, 8)
@@ -946,8 +962,7 @@ static void fill(FusedDesc &f, const smo_tensor &t, int64_t halo_off, int64_t ta
     f.hp = t.hp;
 }
 
-int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaStream_t stream) {
-    (void)ws_bytes;
+int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t flag_bytes, cudaStream_t stream) {
     static thread_local FusedBatch batch;
     static thread_local std::vector<LaunchGroup> groups;
     plan_launches(t, n, groups);
@@ -966,7 +981,7 @@ int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaSt
             batch.strip_start[batch.n + 1] = batch.strip_start[batch.n] + s;
             batch.n++;
         }
-        const int st = dispatch(g.key, batch, max_w, (size_t)halo_off, ws, stream);
+        const int st = dispatch(g.key, batch, max_w, (size_t)halo_off, ws, flag_bytes, stream);
         if (st != SMO_OK) return st;
     }
     return SMO_OK;

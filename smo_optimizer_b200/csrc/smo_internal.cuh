@@ -75,10 +75,20 @@ __device__ __forceinline__ bool bounded_wait_geq(const unsigned int *flag, unsig
     return false;
 }
 
-// fused single-pass path (smo_fused.cu)
+// fused single-pass path (smo_fused.cu).  Workspace: header, then
+// flag_bytes of strip flags (nothing else writes there), then the body.
+struct FusedLayout {
+    size_t flag_bytes;  // strip-ready flags, right after the header
+    size_t body_bytes;  // published rows and head rows, shared with the general path's scratch
+};
 bool fused_takes(const smo_tensor &t);
-size_t fused_workspace_size(const smo_tensor *t, int32_t n);
-int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t ws_bytes, cudaStream_t stream);
+FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n);
+int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t flag_bytes, cudaStream_t stream);
+int64_t wait_limit();
+int64_t set_wait_limit(int64_t polls);
+
+// Checks every descriptor of a step (smo_b200.cu); SMO_OK or the first error.
+int validate_tensors(const smo_tensor *t, int32_t n);
 
 extern thread_local int g_last_cuda_error;
 extern std::atomic<uint64_t> g_launches;

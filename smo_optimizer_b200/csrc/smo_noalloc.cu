@@ -14,6 +14,8 @@
 // process exits.  In host code its name is only a stand-in for the symbol; the
 // device address is obtained per device with cudaGetSymbolAddress (on the first
 // call made with that device current) and that address is what the kernels get.
+// The address is kept for the life of the process: a cudaDeviceReset() unloads
+// the module, so the entry point must not be used on a device after a reset.
 #include <cstdint>
 #include <cstring>
 #include <mutex>
@@ -26,15 +28,16 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = SMO_NO_ALLOC_SCRATCH_BYTES;
-constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) unsigned char g_no_alloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
 
 std::mutex g_setup_mutex;
 void *g_scratch_ptr[kMaxDevices] = {};
 
-// Device address of this device's copy of the scratch array (first call per
-// device resolves it; the device must be current).
+// Device address of this device's copy of the scratch array (the first call
+// per device resolves it; the device must be current).
 int scratch_for_current_device(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -56,10 +59,14 @@ int scratch_for_current_device(void **out) {
 extern "C" int smo_step_no_alloc(const smo_tensor *tensors, int32_t n, int32_t *device_status, void *stream_ptr) {
     if (n < 0 || (n > 0 && !tensors)) return SMO_ERR_INVALID;
     if (n == 0) return SMO_OK;
+    // Every check comes before the shared array is touched: a bad descriptor
+    // or an oversize step changes nothing on the device.
+    int st = smo::validate_tensors(tensors, n);
+    if (st != SMO_OK) return st;
     const size_t need = smo_workspace_size(tensors, n);
     if (need > kNoAllocScratchBytes) return SMO_ERR_WORKSPACE;  // step larger than the fixed scratch
     void *scratch = nullptr;
-    int st = scratch_for_current_device(&scratch);
+    st = scratch_for_current_device(&scratch);
     if (st != SMO_OK) return st;
     cudaStream_t stream = (cudaStream_t)stream_ptr;
     // The array keeps the previous call's contents.  The work counters and the

@@ -58,6 +58,22 @@ def protected_param_groups(named_params, protect_output, quant_capable: bool = T
     return groups
 
 
+def _same_dense_layout(*tensors) -> bool:
+    """True when the tensors share shape and strides and each covers one
+    gap-free span of memory (any dimension order).  An elementwise step can
+    then treat them as flat arrays: the element at memory position k of one is
+    the element at position k of the others."""
+    t0 = tensors[0]
+    if any(t.shape != t0.shape or t.stride() != t0.stride() for t in tensors[1:]):
+        return False
+    expect = 1
+    for stride, size in sorted((st, n) for st, n in zip(t0.stride(), t0.shape) if n != 1):
+        if stride != expect:
+            return False
+        expect *= size
+    return True
+
+
 def _named(params):
     params = list(params)
     if params and isinstance(params[0], tuple) and len(params[0]) == 2 and isinstance(params[0][0], str):
@@ -209,16 +225,56 @@ class _SpatialBase(Optimizer):
             rows[key] = row
         return row
 
+    @staticmethod
+    def _stage(p, grad, state):
+        """The tensors a step hands to the kernels, and the copies back to make
+        after it (None when the kernels work on the real tensors).
+
+        Pooled tensors are contiguous by their init rule.  A dense tensor whose
+        parameter and moments share one gap-free layout (a transposed view, for
+        instance) is stepped in place as flat arrays, its gradient first brought
+        to that layout; any other strided parameter (and a strided quant_only
+        parameter, whose codes follow the logical order) is stepped on
+        contiguous copies that are written back in stream order, so the
+        parameter and its moments are still updated in place as the
+        reference's in-place ops update them (spatial_8bit.py:205-208, 280-283,
+        297)."""
+        if state.get("is_compressed"):
+            return p, (grad if grad.is_contiguous() else grad.contiguous()), state, None
+        if state.get("is_quant_only"):
+            if p.is_contiguous():
+                return p, (grad if grad.is_contiguous() else grad.contiguous()), state, None
+            pc = p.contiguous()
+            return pc, grad.contiguous(), state, [(p, pc)]
+        m, v = state["exp_avg"], state["exp_avg_sq"]
+        if _same_dense_layout(p, m, v):
+            if grad.shape != p.shape or grad.stride() != p.stride():
+                grad = torch.empty_like(p).copy_(grad)  # empty_like keeps the dense layout of p
+            return p, grad, state, None
+        pc, mc, vc = p.contiguous(), m.contiguous(), v.contiguous()
+        st = dict(state)
+        st["exp_avg"], st["exp_avg_sq"] = mc, vc
+        back = [(p, pc)] + [(dst, src) for dst, src in ((m, mc), (v, vc)) if src is not dst]
+        return pc, grad.contiguous(), st, back
+
     def _launch(self, dev, items):
         words = np.empty((len(items), self._ROW_WORDS), dtype=np.uint64)
-        keep = []
+        keep, writeback = [], []
         g0, h0, h1 = self._GRAD_WORD, self._HP_WORD, self._HP_WORD + self._HP_WORDS
         for i, (p, grad, state, group) in enumerate(items):
-            if not grad.is_contiguous():
-                grad = grad.contiguous()
-                keep.append(grad)
-            words[i] = self._row(p, grad, state, group)
-            words[i, g0] = grad.data_ptr()
+            kp, kg, kst, back = self._stage(p, grad, state)
+            if kg is not grad:
+                keep.append(kg)
+            if back is None:
+                words[i] = self._row(kp, kg, kst, group)
+            else:
+                # staged copies change every step: a fresh row, not a cached one
+                rec = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+                self._fill(rec[0], kp, kg, kst, group)
+                words[i] = rec.view(np.uint64).reshape(-1)
+                keep.append((kp, kst))
+                writeback += back
+            words[i, g0] = kg.data_ptr()
             words[i, h0:h1] = self._hyper_words(group, state["step"])[1]
         table = words.view(_lib.TENSOR_DTYPE).reshape(-1)
         with torch.cuda.device(dev):
@@ -229,6 +285,8 @@ class _SpatialBase(Optimizer):
                 self._workspace[dev.index] = ws
             stream = torch.cuda.current_stream(dev).cuda_stream
             _lib.step(table, ws.data_ptr(), ws.numel(), stream)
+            for dst, src in writeback:
+                dst.copy_(src)
         for p, grad, state, group in items:
             self._swap(p, state)
 
@@ -236,7 +294,8 @@ class _SpatialBase(Optimizer):
         pass
 
     def workspace_status(self) -> int:
-        """Device-side status of the last step on each device (synchronises)."""
+        """Device-side status of the steps since the last check, on every device
+        (synchronises; a non-zero status is cleared by reading it)."""
         worst = 0
         lib = _lib.load()
         for idx, ws in self._workspace.items():
@@ -244,6 +303,12 @@ class _SpatialBase(Optimizer):
                 st = lib.smo_workspace_status(ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
             worst = worst or st
         return worst
+
+    def check_device_status(self) -> None:
+        """Raise ``SmoError`` if a step since the last check reported a
+        device-side failure (a bounded inter-CTA wait that ran out); the
+        parameters of that step are then not valid.  Synchronises."""
+        _lib.check(self.workspace_status(), f"{self._name}.step (device status)")
 
 
 class SMO8bit(_SpatialBase):
@@ -409,8 +474,8 @@ class SMO8bit(_SpatialBase):
                 rec[k + "_in"] = state[k].data_ptr()
                 rec[k + "_out"] = s.data_ptr()
         else:
-            if not p.is_contiguous():
-                raise NotImplementedError("non-contiguous dense parameters are not supported")
+            if not _same_dense_layout(p, grad, state["exp_avg"], state["exp_avg_sq"]):
+                raise RuntimeError("dense step: parameter, gradient and moments must share one memory layout")
             rec["kind"] = _lib.SMO_KIND_DENSE
             rec["rows"], rec["cols"] = p.numel(), 1
             rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()
@@ -495,8 +560,8 @@ class SMO(_SpatialBase):
             rec["m_in"], rec["v_in"] = state["exp_avg"].data_ptr(), state["exp_avg_sq"].data_ptr()
             rec["m_out"], rec["v_out"] = sp[0].data_ptr(), sp[1].data_ptr()
         else:
-            if not p.is_contiguous():
-                raise NotImplementedError("non-contiguous dense parameters are not supported")
+            if not _same_dense_layout(p, grad, state["exp_avg"], state["exp_avg_sq"]):
+                raise RuntimeError("dense step: parameter, gradient and moments must share one memory layout")
             rec["kind"] = _lib.SMO_KIND_DENSE
             rec["rows"], rec["cols"] = p.numel(), 1
             rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()

@@ -74,6 +74,12 @@ CASES = {
     "s8_perm": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64,
                                                permute_basis=True),
                     tensors=[((96, 160), 0), ((50, 70), 0)], steps=3, seed=20),
+    # char-LM shapes with bf16-drawn gradients upcast to fp32, the embedding
+    # protected (dense moments) as protect_output=True makes it
+    "s8_bf16_grads": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64),
+                          tensors=[((512, 1536), 0), ((2048, 512), 0), ((512,), 0), ((256, 256), 1)],
+                          groups=[{"compress": True}, {"compress": False}], steps=3, seed=22, bf16=True,
+                          sample_stride=17),
     # SMO-Spatial fp32 pooled moments
     "smo_96x192_k05": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
                            tensors=[((96, 192), 0), ((192,), 0)], steps=5, seed=13),

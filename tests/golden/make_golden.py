@@ -2,15 +2,20 @@
 
 Run once, in a container where the reference checkout exists:
 
-    python tests/golden/make_golden.py [--ref /root/reference] [case ...]
+    python tests/golden/make_golden.py --ref <reference checkout> [case ...]
+
+(or set SMO_REFERENCE_DIR instead of passing --ref).
 
 For every case of cases.py it builds the seeded synthetic params, runs the
 reference's own ``SMO8bit`` / ``SMO`` (smo/optimizers/spatial_8bit.py,
 smo/optimizers/spatial.py) for the case's steps with the seeded synthetic
 grads, and writes ``<case>.npz`` next to this script: the final optimizer
 state arrays, the state metadata, and the final params (a strided sample for
-the large single-weight case).  The tests compare the CPU oracle and the CUDA
-library against these files; nothing at test time imports the reference.
+the large single-weight case).  For the cases in STATE_DICT_CASES it also
+writes ``<case>.state.pt``: the reference optimizer's own ``state_dict()``,
+saved with ``torch.save``, which the tests load into the drop-in optimizer.
+The tests compare the CPU oracle and the CUDA library against these files;
+nothing at test time imports the reference.
 """
 
 from __future__ import annotations
@@ -23,12 +28,16 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+# cases whose final reference state_dict() is saved as written by the reference
+STATE_DICT_CASES = ("s8_groups", "s8_128x256_band_wd", "smo_groups")
 ROOT = os.path.dirname(os.path.dirname(HERE))
 
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    env_ref = os.environ.get("SMO_REFERENCE_DIR")
+    ap.add_argument("--ref", default=env_ref, required=env_ref is None,
+                    help="checkout of the reference (the directory holding the smo package)")
     ap.add_argument("cases", nargs="*")
     args = ap.parse_args()
 
@@ -73,6 +82,10 @@ def main():
             for k in C.STATE_ARRAY_KEYS:
                 if k in st:
                     out[f"{i}.{k}"] = st[k].detach().numpy().copy()
+        if name in STATE_DICT_CASES:
+            sd_path = os.path.join(HERE, f"{name}.state.pt")
+            torch.save(opt.state_dict(), sd_path)
+            print(f"{name}: state_dict {os.path.getsize(sd_path) / 1024:.1f} KiB")
         out["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **out)

@@ -59,6 +59,39 @@ def test_status_strings_and_host_side_validation():
     assert lib.smo_step(t.ctypes.data, 0, addr, 2048, None) == 0           # empty step is a no-op
 
 
+def test_no_alloc_validates_before_touching_its_scratch():
+    """smo_step_no_alloc checks the descriptors first (a bad one returns its
+    own error without any CUDA call, so this runs without a GPU), then the
+    size against its fixed scratch."""
+    lib = _lib.load()
+    t = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    t["kind"] = 99
+    t["param"] = t["grad"] = 256
+    assert lib.smo_step_no_alloc(t.ctypes.data, 1, None, None) == 1        # SMO_ERR_INVALID
+    t["kind"] = _lib.SMO_KIND_DENSE
+    t["cols"] = 1
+    t["param"] = 258
+    assert lib.smo_step_no_alloc(t.ctypes.data, 1, None, None) == 2        # SMO_ERR_ALIGNMENT
+    assert lib.smo_step_no_alloc(t.ctypes.data, 0, None, None) == 0        # empty step
+    # an oversize descriptor that is also invalid reports the invalid field, not the size
+    big = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    big["kind"] = _lib.SMO_KIND_POOLED8
+    big["rows"], big["cols"], big["comp_rows"], big["comp_cols"], big["q_block"] = 8000, 6000, 2400, 1800, 64
+    big["param"] = big["grad"] = 1 << 32                                     # state pointers missing
+    assert lib.smo_step_no_alloc(big.ctypes.data, 1, None, None) == 1
+
+
+def test_wait_limit_setting_round_trips():
+    lib = _lib.load()
+    prev = lib.smo_set_wait_limit(5)
+    try:
+        assert lib.smo_set_wait_limit(0) == 5
+        assert lib.smo_set_wait_limit(-7) == 0
+        assert lib.smo_set_wait_limit(-1) == -1                                # negative = default
+    finally:
+        lib.smo_set_wait_limit(prev)
+
+
 def test_permutation_descriptor_rules():
     """permute_basis index arrays: all four or none, pooled kinds only, no bands."""
     lib = _lib.load()
