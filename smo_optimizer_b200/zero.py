@@ -228,6 +228,24 @@ class Zero1:
         self.exchange_params()
         return loss
 
+    def step_async(self):
+        """``step()`` with the parameter exchange left in flight: the gradient
+        reduce-scatter (``reduce_grads=True``) and the local step are enqueued,
+        the flat all-gather is issued asynchronously, and its work handle is
+        returned (None on one rank, or when the per-tensor broadcast exchange
+        is in use, which completes before returning).  Call ``wait()`` on it
+        before anything reads the parameters (the next forward); host work in
+        between overlaps the exchange."""
+        if self.reduce_grads and self.flat is not None:
+            self.flat.reduce_scatter_grads(self.group, average=self.average_grads)
+        self.local_step()
+        if self.world == 1:
+            return None
+        if self.flat is not None:
+            return self.flat.all_gather(self.group, async_op=True)
+        self.broadcast_params()
+        return None
+
     def zero_grad(self, set_to_none: bool = True):
         if self.reduce_grads and self.flat is not None:
             self.flat.grad_buffer.zero_()  # the gradient views stay bound
@@ -245,3 +263,60 @@ class Zero1:
         """Load this rank's shard (what ``state_dict()`` returned on the same rank)."""
         if self.optimizer is not None:
             self.optimizer.load_state_dict(state_dict)
+
+    def _local_params(self):
+        if self.optimizer is None:
+            return []
+        return [p for g in self.optimizer.param_groups for p in g["params"]]
+
+    def full_state_dict(self, dst: int = 0):
+        """The whole optimizer state in the single-process layout, on rank
+        ``dst`` of the process group (None on the other ranks): ``state`` keyed
+        by each parameter's position in the list given to the constructor and
+        one param group holding all of them, i.e. what the wrapped class returns
+        when one process steps every parameter (for SMO8bit / SMO the
+        reference's layout, smo/optimizers/spatial_8bit.py:155-208).  State
+        tensors are moved to the CPU.  Every rank must call it (one gather)."""
+        index = {id(p): i for i, p in enumerate(self.params)}
+        local = self.state_dict()
+        shard = {}
+        for li, p in enumerate(self._local_params()):
+            st = local["state"].get(li)
+            if st is not None:
+                shard[index[id(p)]] = {k: (v.detach().cpu() if torch.is_tensor(v) else v) for k, v in st.items()}
+        hyper = [{k: v for k, v in g.items() if k != "params"} for g in local["param_groups"]]
+        if len(hyper) > 1:
+            raise ValueError("full_state_dict supports a wrapped optimizer with one param group")
+        if self.world == 1:
+            gathered = [(shard, hyper)]
+        else:
+            root = dist.get_global_rank(self.group, dst) if self.group is not None else dst
+            gathered = [None] * self.world if self.rank == dst else None
+            dist.gather_object((shard, hyper), gathered, dst=root, group=self.group)
+            if self.rank != dst:
+                return None
+        state = {}
+        for sh, _ in gathered:
+            state.update(sh)
+        group = next((h[0] for _, h in gathered if h), {})
+        return {"state": dict(sorted(state.items())),
+                "param_groups": [dict(group, params=list(range(len(self.params))))]}
+
+    def load_full_state_dict(self, state_dict):
+        """Load a single-process state dict (from ``full_state_dict()`` at any
+        world size, or saved by one process stepping every parameter with the
+        wrapped class) into this rank's shard: the entries of the parameters
+        this rank owns under the current partition.  Every rank passes the
+        same dict."""
+        if self.optimizer is None:
+            return
+        index = {id(p): i for i, p in enumerate(self.params)}
+        local = self._local_params()
+        full = state_dict["state"]
+        state = {}
+        for li, p in enumerate(local):
+            gi = index[id(p)]
+            if gi in full:
+                state[li] = full[gi]
+        group = {k: v for k, v in state_dict["param_groups"][0].items() if k != "params"}
+        self.optimizer.load_state_dict({"state": state, "param_groups": [dict(group, params=list(range(len(local))))]})

@@ -6,6 +6,7 @@ The CUDA step cannot run on the CPU, so the ranks use a stand-in optimizer
 (plain SGD on their owned tensors); what is under test is the sharding and the
 collective plumbing around the step."""
 
+import copy
 import os
 import socket
 import time
@@ -28,6 +29,26 @@ class StandIn(torch.optim.Optimizer):
         for g in self.param_groups:
             for p in g["params"]:
                 p.add_(p.grad, alpha=-g["lr"])
+
+
+class StandInMomentum(torch.optim.Optimizer):
+    """Stand-in with per-parameter state (a step count and a moment tensor), so
+    that the sharded state_dict paths have state to gather and scatter."""
+
+    def __init__(self, params, lr=0.1, **_):
+        super().__init__(params, dict(lr=lr))
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        for g in self.param_groups:
+            for p in g["params"]:
+                st = self.state[p]
+                if not st:
+                    st["step"] = 0
+                    st["exp_avg"] = torch.zeros_like(p)
+                st["step"] += 1
+                st["exp_avg"].mul_(0.9).add_(p.grad)
+                p.add_(st["exp_avg"], alpha=-g["lr"])
 
 
 SHAPES = [(64, 256), (128, 128), (32, 32), (300,), (256, 64), (96, 96), (1024,)]
@@ -83,12 +104,41 @@ def _worker(rank, world, port, mode, out):
             pass
 
 
-def _run(mode):
+def _state_worker(rank, world, port, full_in, out):
+    """Three sharded steps, the full state gathered to rank 0; then a fresh
+    Zero1 loads a single-process state dict and takes one more step."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    try:
+        params = [torch.nn.Parameter(t) for t in _params(0)]
+        z = zero.Zero1(params, StandInMomentum, lr=0.5)
+        for step in range(3):
+            for p, g in zip(params, _params(10 + step)):
+                p.grad = g
+            z.step()
+        full = z.full_state_dict()
+        params2 = [torch.nn.Parameter(t.clone()) for t in full_in["params"]]
+        z2 = zero.Zero1(params2, StandInMomentum, lr=0.5)
+        # tensors handed to a spawned process share the parent's storage; the
+        # loaded state is stepped in place, so load a private copy
+        z2.load_full_state_dict(copy.deepcopy(full_in["sd"]))
+        for p, g in zip(params2, _params(13)):
+            p.grad = g
+        z2.step()
+        out[rank] = ("ok", full, [p.detach().clone() for p in params2])
+    except Exception as e:
+        out[rank] = ("error", repr(e), None)
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(mode, target=None, args=()):
     ctx = mp.get_context("spawn")
     mgr = ctx.Manager()
     out = mgr.dict()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, out)) for r in range(2)]
+    target = target or _worker
+    procs = [ctx.Process(target=target, args=(r, 2, port) + (args or (mode,)) + (out,)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
@@ -153,3 +203,34 @@ def test_rank_failure_before_broadcast_surfaces_as_error():
     status = out[0]
     assert status[0] == "error", status
     assert status[2] < 60.0
+
+
+def test_full_state_dict_gathers_and_reloads_across_world_sizes():
+    """full_state_dict() on two ranks equals the state dict of one process
+    stepping every tensor; a single-process state dict loaded into a sharded
+    Zero1 continues exactly as the single process does."""
+    params = [torch.nn.Parameter(t) for t in _params(0)]
+    single = StandInMomentum(params, lr=0.5)
+    for step in range(3):
+        for p, g in zip(params, _params(10 + step)):
+            p.grad = g
+        single.step()
+    sd = copy.deepcopy(single.state_dict())  # state_dict() holds live references
+    snap = [p.detach().clone() for p in params]
+    for p, g in zip(params, _params(13)):
+        p.grad = g
+    single.step()
+    out, codes = _run(None, _state_worker, ({"sd": sd, "params": snap},))
+    assert codes == [0, 0]
+    assert out[0][0] == out[1][0] == "ok", (out[0][1], out[1][1])
+    full = out[0][1]
+    assert out[1][1] is None
+    assert sorted(full["state"]) == list(range(len(SHAPES)))
+    assert full["param_groups"][0]["params"] == list(range(len(SHAPES)))
+    assert full["param_groups"][0]["lr"] == 0.5
+    for i in range(len(SHAPES)):
+        assert full["state"][i]["step"] == sd["state"][i]["step"] == 3
+        assert torch.equal(full["state"][i]["exp_avg"], sd["state"][i]["exp_avg"])
+    for rank in (0, 1):
+        for a, b in zip(out[rank][2], params):
+            assert torch.equal(a, b)
