@@ -137,6 +137,14 @@ SMO_API int smo_workspace_status(void *workspace, void *stream);
  * GPU fault.  No counterpart in the reference. */
 SMO_API int64_t smo_set_wait_limit(int64_t max_polls);
 
+/* Diagnostic for the failure path, process-wide: with on != 0, every
+ * inter-CTA wait of later fused launches waits for a flag value that no strip
+ * publishes, so each runs out its poll limit (smo_set_wait_limit) and the step
+ * reports SMO_ERR_TIMEOUT; its parameters are then not valid.  Every wait
+ * stays bounded, nothing faults.  on = 0 restores normal operation.  Returns
+ * the previous setting.  No counterpart in the reference. */
+SMO_API int smo_inject_wait_timeout(int on);
+
 /* Bytes of the fixed scratch array behind smo_step_no_alloc(). */
 #define SMO_NO_ALLOC_SCRATCH_BYTES ((size_t)32 << 20)
 

@@ -84,6 +84,7 @@ def load():
         "smo_launch_count": (ctypes.c_uint64, []),
         "smo_step_no_alloc": (ctypes.c_int, [P, i32, P, P]),
         "smo_set_wait_limit": (i64, [i64]),
+        "smo_inject_wait_timeout": (ctypes.c_int, [ctypes.c_int]),
     }
     for name, (res, args) in sigs.items():
         fn = getattr(lib, name)

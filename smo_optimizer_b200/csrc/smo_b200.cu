@@ -557,6 +557,8 @@ int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t works
 
 int64_t smo_set_wait_limit(int64_t max_polls) { return set_wait_limit(max_polls); }
 
+int smo_inject_wait_timeout(int on) { return inject_wait_timeout(on); }
+
 int smo_workspace_status(void *workspace, void *stream_ptr) {
     if (!workspace) return SMO_ERR_WORKSPACE;
     cudaStream_t stream = (cudaStream_t)stream_ptr;

@@ -43,7 +43,7 @@
 
 namespace smo {
 
-constexpr int kMaxFusedCtasPerSm = 4;
+constexpr int kMaxFusedCtasPerSm = 6;
 constexpr int kMaxFused = 104;
 constexpr int64_t kStripRows = 16;          // longest strip (compact rows); shorter when a launch has few
 constexpr int64_t kMaxFusedCols = 8192;     // compact columns (shared memory: 24 B per column)
@@ -51,6 +51,9 @@ constexpr int64_t kDefaultWaitIters = 1 << 22;
 
 // Poll limit of the inter-CTA waits (smo_set_wait_limit; negative = default)
 static std::atomic<int64_t> g_wait_limit{-1};
+// Diagnostic: waits look for a flag value that no strip publishes
+// (smo_inject_wait_timeout), so each runs out its poll limit
+static std::atomic<unsigned int> g_wait_skew{0};
 
 int64_t wait_limit() {
     const int64_t v = g_wait_limit.load(std::memory_order_relaxed);
@@ -58,6 +61,8 @@ int64_t wait_limit() {
 }
 
 int64_t set_wait_limit(int64_t polls) { return g_wait_limit.exchange(polls < 0 ? -1 : polls); }
+
+int inject_wait_timeout(int on) { return (int)g_wait_skew.exchange(on ? 1u : 0u); }
 
 // n / d for 32-bit unsigned n by a divisor fixed per tensor: multiply by a
 // precomputed magic number (Granlund-Montgomery / Hacker's Delight 10-1,
@@ -408,6 +413,49 @@ __device__ __forceinline__ void requant_row(const FusedDesc &d, int c, const flo
         requant_block(d, b, c, Rc, Rp, aligned);
 }
 
+// Requantise the int8 blocks that START in compact row c, for the bottom-up
+// row order: a block that runs on into row c+1 (q_block <= w, so at most one
+// more row) finds that row already in the ring (Rn).  Strips start at rows
+// where blocks realign, so no block runs past a strip's last row.
+template <int NT>
+__device__ __forceinline__ void requant_row_up(const FusedDesc &d, int c, const float2 *Rc, const float2 *Rn) {
+    const uint32_t w = (uint32_t)d.w, B = (uint32_t)d.B, C = (uint32_t)d.h * w;
+    const uint32_t rowbase = (uint32_t)c * w, rowend = rowbase + w;
+    const uint32_t b_lo = fast_div(rowbase + B - 1u, d.div_B);
+    const uint32_t b_hi = fast_div(rowend + B - 1u, d.div_B);  // the last row also takes the zero-padded block
+    const bool aligned = (w % B) == 0;                          // blocks never leave the row
+    const int lane = threadIdx.x & 31;
+    for (uint32_t b = b_lo + (threadIdx.x >> 5); b < b_hi; b += NT / 32) {
+        float am = 0.0f, av = 0.0f;
+        for (uint32_t k = lane; k < B; k += 32) {
+            const uint32_t cell = b * B + k;
+            if (cell >= C) break;
+            const float2 mv = (aligned || cell < rowend) ? Rc[cell - rowbase] : Rn[cell - rowend];
+            am = absmax_acc(am, mv.x);
+            av = absmax_acc(av, mv.y);
+        }
+        const float sm = block_scale(warp_absmax(am)), sv = block_scale(warp_absmax(av));
+        const float rm = __frcp_rn(sm), rv = __frcp_rn(sv);
+        const bool finite = sm <= 0x1p126f && sv <= 0x1p126f;  // uniform across the warp; false for NaN
+        for (uint32_t k = lane; k < B; k += 32) {
+            const uint32_t cell = b * B + k;
+            float2 mv = f2(0.0f, 0.0f);
+            if (cell < C) mv = (aligned || cell < rowend) ? Rc[cell - rowbase] : Rn[cell - rowend];
+            if (finite) {
+                d.mq_out[cell] = quantize_finite(mv.x, sm, rm);
+                d.vq_out[cell] = quantize_finite(mv.y, sv, rv);
+            } else {
+                d.mq_out[cell] = quantize_rc(mv.x, sm, rm);
+                d.vq_out[cell] = quantize_rc(mv.y, sv, rv);
+            }
+        }
+        if (lane == 0) {
+            d.ms_out[b] = sm;
+            d.vs_out[b] = sv;
+        }
+    }
+}
+
 struct RowCo {
     int s0, s1;  // ring-relative rows (0: c-1, 1: c, 2: c+1)
     float l0, l1;
@@ -558,16 +606,32 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
     }
 }
 
-// One strip: phase-1 rows r = c0 .. c1 (c1 = look-ahead row, when it exists),
-// each followed by phase 2 of row r-1; then the strip's first row.
+// Barrier of the NT threads that run the row pipeline (named barrier 1: in the
+// staged kernel the producer warp is not part of it).
+template <int NT>
+__device__ __forceinline__ void cta_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
+}
+
+// One strip of compact rows [c0, c1), processed bottom-up: phase 1 of row r
+// (from the look-ahead row c1, the next strip's first row, when it exists,
+// down to c0), each followed by phase 2 of row r+1, which then has all three
+// of its rows in the ring.  The look-ahead row is read first and the strip's
+// bottom row c1-1 is published for the next strip right after it, so the
+// flag the next strip waits on is set at the start of this strip's work;
+// the strip's top row c0 needs the previous strip's published bottom row and
+// is written last, after a bounded acquire wait that has normally long been
+// satisfied.  Row c0 is also the look-ahead row of the previous strip, whose
+// read of its OLD parameters is covered by the same flag: it is written only
+// after the wait.
 template <int KH, int KW, int CELLS, int NT>
 __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsigned int epoch, float2 *ring,
-                              float2 *head, RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
-                              int64_t wait_iters) {
+                              RowCo (*rowco)[KH], WsHeader *hdr, unsigned int *flags, float *halo,
+                              int64_t wait_iters, unsigned int wait_skew) {
     const int w = d.w, h = d.h;
     const int c0 = sidx * d.L;
     const int c1 = c0 + d.L < h ? c0 + d.L : h;
-    const int last = c1 < h ? c1 : c1 - 1;  // last phase-1 row
+    const int top = c1 < h ? c1 : c1 - 1;  // first phase-1 row
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
     AdamK ak;
     ak.sbc2 = splat(d.hp.sqrt_bc2);
@@ -578,73 +642,53 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
     ak.fast = d.hp.eps >= 0x1p-27f;
     auto RR = [&](int c) { return ring + (c % 3) * w; };
     float2 *pub = reinterpret_cast<float2 *>(halo + d.halo_off) + (int64_t)sidx * w;
-    // rows c0 and c0+1 are kept in this CTA's global head buffer (L2) until the
-    // strip's first row is written at the end
-    auto save_head = [&](int c, int slot) {
-        const float2 *src = RR(c);
-        float2 *dst = head + slot * w;
-        for (int j = threadIdx.x; j < w; j += NT) __stcg(dst + j, src[j]);
-    };
 
-    for (int r = c0; r <= last; r++) {
-        const bool do2 = r - 1 > c0;  // phase 2 of row r-1 in this iteration
-        if (do2) compute_rowco<KH>(d, r - 1, rowco[(r - 1) & 1]);
+    for (int r = top; r >= c0; r--) {
+        const bool do2 = r + 1 < c1;  // phase 2 of row r+1 (an own row) in this iteration
+        if (do2) compute_rowco<KH>(d, r + 1, rowco[(r + 1) & 1]);
         phase1<KH, KW, CELLS, NT>(d, r, RR(r), r < c1);
-        __syncthreads();
+        cta_sync<NT>();
         if (r < c1) {
-            if (q8) requant_row<NT>(d, r, RR(r), r > c0 ? RR(r - 1) : nullptr);
-            if (r == c0) save_head(r, 0);
-            if (r == c0 + 1) save_head(r, 1);
-        } else {
-            // look-ahead row: keep it as the strip's second row if the strip has
-            // one row, then publish this strip's last row for the next strip
-            // (after the look-ahead read of that strip's parameters and state)
-            if (r == c0 + 1) save_head(r, 1);
-            const float2 *src = RR(c1 - 1);
-            for (int j = threadIdx.x; j < w; j += NT) __stcg(pub + j, src[j]);
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                __threadfence();
-                store_release(flags + gstrip, epoch);
+            if (q8) requant_row_up<NT>(d, r, RR(r), r + 1 < c1 ? RR(r + 1) : nullptr);
+            if (r == c1 - 1 && c1 < h) {
+                // publish the bottom row for the next strip, after the
+                // look-ahead read of that strip's first row (previous iteration)
+                const float2 *src = RR(r);
+                for (int j = threadIdx.x; j < w; j += NT) __stcg(pub + j, src[j]);
+                cta_sync<NT>();
+                if (threadIdx.x == 0) {
+                    __threadfence();
+                    store_release(flags + gstrip, epoch);
+                }
             }
         }
         if (do2) {
-            const float2 *R[3] = {RR(r - 2), RR(r - 1), RR(r)};
-            phase2<KH, KW, NT>(d, r - 1, R, rowco[(r - 1) & 1], ak);
+            const float2 *R[3] = {RR(r), RR(r + 1), r + 2 <= top ? RR(r + 2) : RR(r + 1)};
+            phase2<KH, KW, NT>(d, r + 1, R, rowco[(r + 1) & 1], ak);
         }
-        __syncthreads();
-    }
-    if (c1 == h && c1 - 1 > c0) {
-        // the tensor's last row: no look-ahead row below it
-        compute_rowco<KH>(d, c1 - 1, rowco[(c1 - 1) & 1]);
-        __syncthreads();
-        const float2 *R[3] = {RR(c1 - 2), RR(c1 - 1), RR(c1 - 1)};
-        phase2<KH, KW, NT>(d, c1 - 1, R, rowco[(c1 - 1) & 1], ak);
-        __syncthreads();
+        cta_sync<NT>();
     }
 
-    // deferred first row: rows c0-1 (the previous strip's published row), c0
-    // and c0+1 go back into ring slots 0, 1, 2
+    // row c0: its upper neighbour is the previous strip's published bottom row
     __shared__ int s_ok;
     compute_rowco<KH>(d, c0, rowco[c0 & 1]);
     if (c0 > 0 && threadIdx.x == 0) {
-        const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch, wait_iters, &hdr->error);
+        const bool ok = bounded_wait_eq(flags + gstrip - 1, epoch + wait_skew, wait_iters, &hdr->error);
         if (!ok) report_error(hdr, SMO_ERR_TIMEOUT, (unsigned int)gstrip);
         s_ok = ok;
     }
-    __syncthreads();
-    const float2 *prev = pub - (sidx > 0 ? w : 0);
-    const bool ok = c0 > 0 && s_ok;
-    const bool next = c0 + 1 < h;
-    for (int j = threadIdx.x; j < w; j += NT) {
-        if (c0 > 0) ring[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
-        ring[w + j] = __ldcg(head + j);
-        if (next) ring[2 * w + j] = __ldcg(head + w + j);
+    cta_sync<NT>();
+    if (c0 > 0) {
+        // the ring slot of row c0-1 holds row c0+2, which is no longer needed
+        const float2 *prev = pub - w;
+        float2 *dst = RR(c0 - 1);
+        const bool ok = s_ok;
+        for (int j = threadIdx.x; j < w; j += NT) dst[j] = ok ? __ldcg(prev + j) : f2(0.0f, 0.0f);
+        cta_sync<NT>();
     }
-    __syncthreads();
-    const float2 *R[3] = {c0 > 0 ? ring : ring + w, ring + w, next ? ring + 2 * w : ring + w};
+    const float2 *R[3] = {c0 > 0 ? RR(c0 - 1) : RR(c0), RR(c0), c0 + 1 <= top ? RR(c0 + 1) : RR(c0)};
     phase2<KH, KW, NT>(d, c0, R, rowco[c0 & 1], ak);
-    __syncthreads();
+    cta_sync<NT>();
 }
 
 __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s) {
@@ -659,13 +703,12 @@ __device__ __forceinline__ int find_strip_tensor(const FusedBatch &b, int64_t s)
 template <int KH, int KW, int CELLS, int NT, int MINB>
 __global__ void __launch_bounds__(NT, MINB)
     fused_step_kernel(const __grid_constant__ FusedBatch b, WsHeader *hdr, unsigned int *flags, float *halo,
-                      float *heads, int64_t head_stride, int64_t wait_iters) {
+                      int64_t wait_iters, unsigned int wait_skew) {
     extern __shared__ float2 ring[];
     __shared__ RowCo rowco[2][KH];
     __shared__ int64_t s_strip;
     __shared__ unsigned int s_epoch;
     if (threadIdx.x == 0) s_epoch = *(volatile unsigned int *)&hdr->epoch + 1u;
-    float2 *head = reinterpret_cast<float2 *>(heads + (int64_t)blockIdx.x * head_stride);
     const int64_t total = b.strip_start[b.n];
     for (;;) {
         if (threadIdx.x == 0) s_strip = (int64_t)atomicAdd(&hdr->next_item, 1u);
@@ -675,8 +718,8 @@ __global__ void __launch_bounds__(NT, MINB)
         __syncthreads();
         if (s >= total) break;
         const int t = find_strip_tensor(b, s);
-        process_strip<KH, KW, CELLS, NT>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, head, rowco, hdr, flags,
-                                         halo, wait_iters);
+        process_strip<KH, KW, CELLS, NT>(b.d[t], (int)(s - b.strip_start[t]), s, epoch, ring, rowco, hdr, flags,
+                                         halo, wait_iters, wait_skew);
     }
     if (threadIdx.x == 0) {
         __threadfence();
@@ -760,24 +803,26 @@ static int window_key(const smo_tensor &t) {
     return (int)((t.rows / t.comp_rows) * 16 + (t.cols / t.comp_cols));
 }
 
-// CTA width of a launch: 256 or 384 threads, whichever leaves fewer idle
-// thread-columns over the batch's compact rows (a compact row of w cells takes
-// ceil(w / NT) passes of NT threads); ties go to 384.  SMO_B200_FUSED_THREADS
-// (256 or 384) forces one width, for measurements.
+// CTA width of a launch: 192 threads (four CTAs of 80 registers per SM, so
+// four independent row pipelines hide each other's load latency), or 256 when
+// that leaves fewer idle thread-columns over the batch's compact rows (a
+// compact row of w cells takes ceil(w / NT) passes of NT threads).
+// SMO_B200_FUSED_THREADS (128, 192, 256 or 384) forces one width, for
+// measurements.
 static int pick_threads(const FusedBatch &b) {
     static int forced = -1;
     if (forced < 0) {
         const char *e = getenv("SMO_B200_FUSED_THREADS");
         forced = e ? atoi(e) : 0;
     }
-    if (forced == 256 || forced == 384) return forced;
-    int64_t idle256 = 0, idle384 = 0;
+    if (forced == 128 || forced == 192 || forced == 256 || forced == 384) return forced;
+    int64_t idle192 = 0, idle256 = 0;
     for (int i = 0; i < b.n; i++) {
         const int64_t w = b.d[i].w, rows = b.d[i].h;
+        idle192 += rows * ((w + 191) / 192 * 192 - w);
         idle256 += rows * ((w + 255) / 256 * 256 - w);
-        idle384 += rows * ((w + 383) / 384 * 384 - w);
     }
-    return idle384 <= idle256 ? 384 : 256;
+    return idle256 < idle192 ? 256 : 192;
 }
 
 constexpr int kMaxDevices = 64;
@@ -806,8 +851,8 @@ static inline size_t align_up(size_t x) { return (x + kScratchAlign - 1) / kScra
 // order (at most kMaxFused per launch), each group with its strip length.
 // Short launches get shorter strips so that every CTA slot sees several
 // strips (the last strips of a launch otherwise leave SMs idle): the longest
-// of 16, 8, 4 rows that gives at least 5 strips per CTA slot of a 2-CTA/SM
-// grid (measured best between 5 and 10 strips per CTA).
+// of 16, 8, 4 rows that gives at least 5 strips per CTA slot of a 4-CTA/SM
+// grid.
 struct LaunchGroup {
     int key;
     int64_t target_rows;
@@ -820,7 +865,7 @@ static void plan_launches(const smo_tensor *t, int32_t n, std::vector<LaunchGrou
     out.clear();
     std::vector<char> done((size_t)n);
     for (int32_t i = 0; i < n; i++) done[i] = !fused_takes(t[i]);
-    const int64_t want = 5 * 2 * (int64_t)device_sm_count();
+    const int64_t want = 5 * 4 * (int64_t)device_sm_count();
     for (int32_t i = 0; i < n; i++) {
         if (done[i]) continue;
         LaunchGroup g;
@@ -842,8 +887,8 @@ static void plan_launches(const smo_tensor *t, int32_t n, std::vector<LaunchGrou
 }
 
 // Workspace after the header: [flags: one word per strip][published rows:
-// 2*w floats per strip][head rows: 4*max_w floats per CTA].  Sized for the
-// whole set; each window-group launch reuses the space.  The flag words sit
+// 2*w floats per strip].  Sized for the largest window-group launch of the
+// set; each launch reuses the space.  The flag words sit
 // in a region of their own that nothing else writes (the general path's
 // scratch starts after it): a flag word may only ever hold a launch epoch,
 // or a stale float could read as "strip published".
@@ -851,18 +896,15 @@ FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n) {
     std::vector<LaunchGroup> groups;
     plan_launches(t, n, groups);
     FusedLayout out{0, 0};
-    const size_t ctas = (size_t)device_sm_count() * kMaxFusedCtasPerSm;
     for (const LaunchGroup &g : groups) {
         size_t strips = 0, halo_floats = 0;
-        int64_t max_w = 0;
         for (int32_t k : g.members) {
             const int64_t s = num_strips(t[k], g.target_rows);
             strips += (size_t)s;
             halo_floats += (size_t)s * 2 * (size_t)t[k].comp_cols;
-            max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
         }
         const size_t flags = align_up(strips * sizeof(unsigned int));
-        const size_t body = align_up(halo_floats * sizeof(float)) + ctas * 4 * (size_t)max_w * sizeof(float);
+        const size_t body = align_up(halo_floats * sizeof(float));
         out.flag_bytes = out.flag_bytes > flags ? out.flag_bytes : flags;
         out.body_bytes = out.body_bytes > body ? out.body_bytes : body;
     }
@@ -870,61 +912,74 @@ FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n) {
 }
 
 // The kernel instance of a window shape and CTA width: 16-element windows take
-// one cell per thread-iteration, smaller windows two; 384-thread CTAs run two
-// per SM (80 registers), 256-thread CTAs four (one cell, 64 registers) or
-// three (two cells, 80 registers).
+// one cell per thread-iteration, smaller windows two; 128-, 192- and
+// 384-thread CTAs run six, four and two per SM at 80 registers, 256-thread
+// CTAs four (one cell, 64 registers) or three (two cells, 80 registers).
 template <int KH, int KW>
 static auto fused_kernel_for(int nt) {
     constexpr int kCells = KH * KW >= 16 ? 1 : 2;
     constexpr int kMinBlocks256 = kCells == 1 ? 4 : 3;
-    return nt == 384 ? fused_step_kernel<KH, KW, kCells, 384, 2> : fused_step_kernel<KH, KW, kCells, 256, kMinBlocks256>;
+    switch (nt) {
+        case 128: return fused_step_kernel<KH, KW, kCells, 128, 6>;
+        case 192: return fused_step_kernel<KH, KW, kCells, 192, 4>;
+        case 384: return fused_step_kernel<KH, KW, kCells, 384, 2>;
+        default: return fused_step_kernel<KH, KW, kCells, 256, kMinBlocks256>;
+    }
+}
+
+static int kernel_cache_slot(int nt) { return nt == 384 ? 1 : nt == 192 ? 4 : nt == 128 ? 5 : 0; }
+
+// The shared-memory attribute and the occupancy of a kernel instance are set
+// and queried once per device and size (the attribute is a maximum, so a
+// larger earlier setting covers smaller launches).
+struct KernelCache {
+    size_t smem_attr = 0, smem_occ = 0;
+    int per_sm = 0;
+};
+
+template <class Kern>
+static int occupancy(Kern kern, KernelCache &c, int nt, size_t smem, int &per_sm) {
+    cudaError_t e = cudaSuccess;
+    if (smem > c.smem_attr) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+        c.smem_attr = smem;
+    }
+    if (c.per_sm == 0 || c.smem_occ != smem) {
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c.per_sm, kern, nt, smem);
+        if (e != cudaSuccess) return (c.per_sm = 0, g_last_cuda_error = (int)e, SMO_ERR_CUDA);
+        c.smem_occ = smem;
+    }
+    per_sm = c.per_sm;
+    return SMO_OK;
 }
 
 template <int KH, int KW>
 static int launch_fused_group(FusedBatch &b, int64_t max_w, size_t halo_floats, char *ws, size_t flag_bytes,
                               cudaStream_t stream) {
-    const size_t smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
-    const int nt = pick_threads(b);
-    auto kern = fused_kernel_for<KH, KW>(nt);
-    // The shared-memory attribute and the occupancy of this kernel instance
-    // are set and queried once per device and size (the attribute is a
-    // maximum, so a larger earlier setting covers smaller launches).
-    struct Cache {
-        size_t smem_attr = 0, smem_occ = 0;
-        int per_sm = 0;
-    };
-    static Cache cache[kMaxDevices][2];
+    static KernelCache cache[kMaxDevices][6];
     static std::mutex mu;
     const int dev = current_device();
-    int per_sm = 0;
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        Cache scratch;
-        Cache &c = dev >= 0 ? cache[dev][nt == 384] : scratch;
-        cudaError_t e = cudaSuccess;
-        if (smem > c.smem_attr) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
-            c.smem_attr = smem;
-        }
-        if (c.per_sm == 0 || c.smem_occ != smem) {
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c.per_sm, kern, nt, smem);
-            if (e != cudaSuccess) return (c.per_sm = 0, g_last_cuda_error = (int)e, SMO_ERR_CUDA);
-            c.smem_occ = smem;
-        }
-        per_sm = c.per_sm;
-    }
-    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
-    const int64_t strips = b.strip_start[b.n];
-    int64_t grid = (int64_t)device_sm_count() * per_sm;
-    grid = grid < strips ? grid : strips;
     WsHeader *hdr = (WsHeader *)ws;
     unsigned int *flags = (unsigned int *)(ws + kWsHeader);
-    char *body = ws + kWsHeader + flag_bytes;
-    float *halo = (float *)body;
-    body += align_up(halo_floats * sizeof(float));
-    float *heads = (float *)body;
-    kern<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, heads, 4 * max_w, wait_limit());
+    float *halo = (float *)(ws + kWsHeader + flag_bytes);
+    const int64_t strips = b.strip_start[b.n];
+    size_t smem = 0;
+    int nt = 0, per_sm = 0, st = SMO_OK;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        KernelCache scratch;
+        smem = (size_t)6 * max_w * sizeof(float);  // ring: 3 rows x (m, v)
+        nt = pick_threads(b);
+        st = occupancy(fused_kernel_for<KH, KW>(nt), dev >= 0 ? cache[dev][kernel_cache_slot(nt)] : scratch, nt, smem,
+                       per_sm);
+    }
+    if (st != SMO_OK) return st;
+    per_sm = per_sm < 1 ? 1 : (per_sm > kMaxFusedCtasPerSm ? kMaxFusedCtasPerSm : per_sm);
+    int64_t grid = (int64_t)device_sm_count() * per_sm;
+    grid = grid < strips ? grid : strips;
+    fused_kernel_for<KH, KW>(nt)<<<(unsigned)grid, nt, smem, stream>>>(b, hdr, flags, halo, wait_limit(),
+                                                                     g_wait_skew.load(std::memory_order_relaxed));
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return (g_last_cuda_error = (int)e, SMO_ERR_CUDA);
     g_launches++;

@@ -86,6 +86,7 @@ FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n);
 int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t flag_bytes, cudaStream_t stream);
 int64_t wait_limit();
 int64_t set_wait_limit(int64_t polls);
+int inject_wait_timeout(int on);
 
 // Checks every descriptor of a step (smo_b200.cu); SMO_OK or the first error.
 int validate_tensors(const smo_tensor *t, int32_t n);

@@ -10,10 +10,10 @@
 * The fused kernel's strip-ready flags live in a region nothing else writes:
   general-path scratch holding float bit patterns equal to the next launch
   epoch does not disturb the next step.
-* The fused kernel's own bounded wait, with its poll limit set to zero on a
-  many-strip tensor: the launch returns, the device status reports
-  SMO_ERR_TIMEOUT, the optimizer raises, and a step after the limit is
-  restored is correct again.
+* The fused kernel's own bounded wait, made to wait for a flag value that no
+  strip publishes, with a short poll limit, on a many-strip tensor: the launch
+  returns, the device status reports SMO_ERR_TIMEOUT, the optimizer raises,
+  and a step after normal operation is restored is correct again.
 """
 
 import copy
@@ -152,11 +152,13 @@ def test_fused_wait_timeout_reports_and_recovers():
 
     g2 = synthetic.synth_grad(41, 2, 0, shape)
     p.grad = torch.from_numpy(g2).cuda()
-    prev = lib.smo_set_wait_limit(0)
+    prev = lib.smo_set_wait_limit(1000)
+    prev_inject = lib.smo_inject_wait_timeout(1)
     try:
-        opt.step()                      # every strip after the first polls its flag once
+        opt.step()                      # every strip after the first waits for a flag nothing sets
         torch.cuda.synchronize()        # the launch returns
     finally:
+        lib.smo_inject_wait_timeout(prev_inject)
         lib.smo_set_wait_limit(prev)
     with pytest.raises(_lib.SmoError, match="bounded device wait timed out"):
         opt.check_device_status()

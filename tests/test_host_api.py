@@ -90,6 +90,8 @@ def test_wait_limit_setting_round_trips():
         assert lib.smo_set_wait_limit(-1) == -1                                # negative = default
     finally:
         lib.smo_set_wait_limit(prev)
+    assert lib.smo_inject_wait_timeout(1) == 0
+    assert lib.smo_inject_wait_timeout(0) == 1
 
 
 def test_permutation_descriptor_rules():
