@@ -528,6 +528,24 @@ __device__ __forceinline__ void width_pass3(const float2 *const R[3], int j, int
     }
 }
 
+// The same width pass for a cell with j > 0 (every cell but a row's first):
+// no edge selects.
+template <int KW>
+__device__ __forceinline__ void width_pass3_inner(const float2 *const R[3], int j, int w, float2 (&h)[3][KW]) {
+    const int jr = j + 1 < w ? j + 1 : w - 1;
+#pragma unroll
+    for (int s = 0; s < 3; s++) {
+        const float2 left = R[s][j - 1], mid = R[s][j], right = R[s][jr];
+#pragma unroll
+        for (int t = 0; t < KW; t++) {
+            if (t < KW / 2)
+                h[s][t] = __ffma2_rn(left, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(mid, splat(col_l1<KW>(t))));
+            else
+                h[s][t] = __ffma2_rn(mid, splat(1.0f - col_l1<KW>(t)), __fmul2_rn(right, splat(col_l1<KW>(t))));
+        }
+    }
+}
+
 // Rows of cell j (bits of `rows`) whose fast Adam write failed its range
 // check: recomputed with the IEEE operations from the untouched parameters.
 template <int KH, int KW>
@@ -562,10 +580,14 @@ __device__ __noinline__ void phase2_fixup(const FusedDesc &d, int c, int j, cons
 
 // Phase 2 of compact row c: the KH parameter rows, from the post-EMA rows
 // c-1 (R[0]), c (R[1]), c+1 (R[2]) in shared memory (an absent neighbour row
-// is passed as row c and never weighted).  Row weights come from `rowco`.
-// Every element takes the FMA-only Adam write; a row whose range check fails
-// is not stored and goes to phase2_fixup.
-template <int KH, int KW, int NT>
+// is passed as row c and never weighted).  Row weights come from `rowco`; for
+// an INTERIOR row (0 < c < h-1) they are compile-time constants instead:
+// output row i interpolates rows (c-1, c) with weight row_l1(i) on row c for
+// i < KH/2 and rows (c, c+1) for i >= KH/2, which is what compute_rowco
+// yields there, exactly (also inside low_peak bands, whose one-row halo keeps
+// interior rows interior).  Every element takes the FMA-only Adam write; a row
+// whose range check fails is not stored and goes to phase2_fixup.
+template <int KH, int KW, int NT, bool INTERIOR>
 __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
                                        const AdamK &ak) {
     const int w = d.w;
@@ -576,26 +598,39 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
 #pragma unroll
         for (int i = 0; i < KH; i++) load_param_row<KW, true>(pbase + i * W, pv[i]);
         float2 h[3][KW];
-        width_pass3<KW>(R, j, w, h);
+        if (j > 0) width_pass3_inner<KW>(R, j, w, h);
+        else width_pass3<KW>(R, j, w, h);
         unsigned fail = 0;
 #pragma unroll
         for (int i = 0; i < KH; i++) {
-            const RowCo rc = rowco[i];
-            const bool lo0 = rc.s0 == 0, lo1 = rc.s1 == 1;  // uniform across the CTA
             float2 mh[KW];
+            if constexpr (INTERIOR) {
+                const bool upper = i < KH / 2;  // resolved at compile time once the loop is unrolled
 #pragma unroll
-            for (int t = 0; t < KW; t++) {
-                const float2 a = lo0 ? h[0][t] : h[1][t];
-                const float2 b = lo1 ? h[1][t] : h[2][t];
-                mh[t] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
+                for (int t = 0; t < KW; t++)
+                    mh[t] = __ffma2_rn(upper ? h[0][t] : h[1][t], splat(1.0f - col_l1<KH>(i)),
+                                       __fmul2_rn(upper ? h[1][t] : h[2][t], splat(col_l1<KH>(i))));
+            } else {
+                const RowCo rc = rowco[i];
+                const bool lo0 = rc.s0 == 0, lo1 = rc.s1 == 1;  // uniform across the CTA
+#pragma unroll
+                for (int t = 0; t < KW; t++) {
+                    const float2 a = lo0 ? h[0][t] : h[1][t];
+                    const float2 b = lo1 ? h[1][t] : h[2][t];
+                    mh[t] = __ffma2_rn(a, splat(rc.l0), __fmul2_rn(b, splat(rc.l1)));
+                }
             }
             bool ok = ak.fast;
             float pn[KW];
 #pragma unroll
             for (int t = 0; t < KW; t += 2) {
+                // clamp(v, min=0) as a NaN-propagating max: it differs from
+                // clamp_min0 only by giving +0 for -0, and a zero v always
+                // fails the fast path's range check, whose IEEE fix-up then
+                // clamps with clamp_min0 itself
                 float2 o;
                 ok &= adam_write2_fast(f2(pv[i][t], pv[i][t + 1]), f2(mh[t].x, mh[t + 1].x),
-                                       f2(clamp_min0(mh[t].y), clamp_min0(mh[t + 1].y)), ak, o);
+                                       f2(nan_max(mh[t].y, 0.0f), nan_max(mh[t + 1].y, 0.0f)), ak, o);
                 pn[t] = o.x;
                 pn[t + 1] = o.y;
             }
@@ -606,8 +641,14 @@ __device__ __forceinline__ void phase2(const FusedDesc &d, int c, const float2 *
     }
 }
 
-// Barrier of the NT threads that run the row pipeline (named barrier 1: in the
-// staged kernel the producer warp is not part of it).
+template <int KH, int KW, int NT>
+__device__ __forceinline__ void phase2_row(const FusedDesc &d, int c, const float2 *const R[3], const RowCo *rowco,
+                                           const AdamK &ak) {
+    if (c > 0 && c < d.h - 1) phase2<KH, KW, NT, true>(d, c, R, rowco, ak);
+    else phase2<KH, KW, NT, false>(d, c, R, rowco, ak);
+}
+
+// Barrier of the NT threads that run the row pipeline (named barrier 1).
 template <int NT>
 __device__ __forceinline__ void cta_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(NT) : "memory");
@@ -664,7 +705,7 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         }
         if (do2) {
             const float2 *R[3] = {RR(r), RR(r + 1), r + 2 <= top ? RR(r + 2) : RR(r + 1)};
-            phase2<KH, KW, NT>(d, r + 1, R, rowco[(r + 1) & 1], ak);
+            phase2_row<KH, KW, NT>(d, r + 1, R, rowco[(r + 1) & 1], ak);
         }
         cta_sync<NT>();
     }
@@ -687,7 +728,7 @@ __device__ void process_strip(const FusedDesc &d, int sidx, int64_t gstrip, unsi
         cta_sync<NT>();
     }
     const float2 *R[3] = {c0 > 0 ? RR(c0 - 1) : RR(c0), RR(c0), c0 + 1 <= top ? RR(c0 + 1) : RR(c0)};
-    phase2<KH, KW, NT>(d, c0, R, rowco[c0 & 1], ak);
+    phase2_row<KH, KW, NT>(d, c0, R, rowco[c0 & 1], ak);
     cta_sync<NT>();
 }
 
