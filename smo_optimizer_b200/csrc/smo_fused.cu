@@ -32,6 +32,7 @@
 //
 // The parameter rows read in phase 1 are read again in phase 2 one pipeline
 // step later; that second read is meant to hit L2.
+#include <algorithm>
 #include <atomic>
 #include <cstdlib>
 #include <cstring>
@@ -889,15 +890,16 @@ static int device_sm_count() {
 static inline size_t align_up(size_t x) { return (x + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
 
 // Launch plan: tensors the fused kernel takes, grouped by window shape in scan
-// order (at most kMaxFused per launch), each group with its strip length.
+// order (at most kMaxFused per launch), ordered by row width within a group,
+// each with its strip length.
 // Short launches get shorter strips so that every CTA slot sees several
 // strips (the last strips of a launch otherwise leave SMs idle): the longest
 // of 16, 8, 4 rows that gives at least 5 strips per CTA slot of a 4-CTA/SM
 // grid.
 struct LaunchGroup {
     int key;
-    int64_t target_rows;
     std::vector<int32_t> members;
+    std::vector<int64_t> target;  // strip length target of each member
 };
 
 static int device_sm_count();
@@ -916,13 +918,18 @@ static void plan_launches(const smo_tensor *t, int32_t n, std::vector<LaunchGrou
             g.members.push_back(k);
             done[k] = 1;
         }
-        g.target_rows = kStripRows;
-        while (g.target_rows > 4) {
+        // widest rows first: the largest strips are taken early and the
+        // launch ends on the smallest ones, which shortens its tail
+        std::stable_sort(g.members.begin(), g.members.end(),
+                         [&](int32_t a, int32_t b) { return t[a].cols > t[b].cols; });
+        int64_t rows = kStripRows;
+        while (rows > 4) {
             int64_t strips = 0;
-            for (int32_t k : g.members) strips += num_strips(t[k], g.target_rows);
+            for (int32_t k : g.members) strips += num_strips(t[k], rows);
             if (strips >= want) break;
-            g.target_rows /= 2;
+            rows /= 2;
         }
+        g.target.assign(g.members.size(), rows);
         out.push_back(std::move(g));
     }
 }
@@ -939,8 +946,9 @@ FusedLayout fused_workspace_layout(const smo_tensor *t, int32_t n) {
     FusedLayout out{0, 0};
     for (const LaunchGroup &g : groups) {
         size_t strips = 0, halo_floats = 0;
-        for (int32_t k : g.members) {
-            const int64_t s = num_strips(t[k], g.target_rows);
+        for (size_t m = 0; m < g.members.size(); m++) {
+            const int32_t k = g.members[m];
+            const int64_t s = num_strips(t[k], g.target[m]);
             strips += (size_t)s;
             halo_floats += (size_t)s * 2 * (size_t)t[k].comp_cols;
         }
@@ -1068,10 +1076,11 @@ int fused_step(const smo_tensor *t, int32_t n, char *ws, size_t flag_bytes, cuda
         batch.n = 0;
         batch.strip_start[0] = 0;
         int64_t halo_off = 0, max_w = 0;
-        for (int32_t k : g.members) {
+        for (size_t m = 0; m < g.members.size(); m++) {
+            const int32_t k = g.members[m];
             FusedDesc &f = batch.d[batch.n];
-            fill(f, t[k], halo_off, g.target_rows);
-            const int64_t s = num_strips(t[k], g.target_rows);
+            fill(f, t[k], halo_off, g.target[m]);
+            const int64_t s = num_strips(t[k], g.target[m]);
             halo_off += s * 2 * t[k].comp_cols;
             max_w = max_w > t[k].comp_cols ? max_w : t[k].comp_cols;
             batch.strip_start[batch.n + 1] = batch.strip_start[batch.n] + s;
