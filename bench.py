@@ -51,6 +51,10 @@ def parse_args():
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="one process: step only the share of the tensors that rank --shard-rank owns "
+                         "when the set is split ZeRO-1 style over this many ranks (per-rank profiling)")
+    ap.add_argument("--shard-rank", type=int, default=0)
     return ap.parse_args()
 
 
@@ -64,12 +68,16 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def load_traffic(workload, kernel):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+def load_traffic(workload, kernel, world=1, rank=0):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary: the whole set at one GPU, or rank ``rank``'s share when the set
+    is split over ``world`` ranks (``<workload>@<world>`` entries)."""
     path = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(path) as f:
             data = json.load(f)
+        if world > 1:
+            return data[f"{workload}@{world}"][str(rank)]
         return data[workload][kernel]
     except Exception:
         return None
@@ -420,8 +428,14 @@ def main():
 
     shapes = [s for _, s in wl.tensors]
     costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64)) for s in shapes]
-    owner = zero.lpt_partition(costs, world)
-    owned = [o == rank for o in owner]
+    shard_of = args.shard_of if world == 1 and args.shard_of > 1 else 0
+    if shard_of:
+        # one rank's share of a ZeRO-1 split, stepped alone on this GPU
+        owner = zero.lpt_partition(costs, shard_of)
+        owned = [o == args.shard_rank for o in owner]
+    else:
+        owner = zero.lpt_partition(costs, world)
+        owned = [o == rank for o in owner]
     # N > 1: every rank holds every gradient (a replicated model's backward), which
     # the gradient reduce-scatter timing below needs; the local step reads only
     # the owned ones
@@ -490,12 +504,15 @@ def main():
         raise RuntimeError(f"device status {status} after the timed region")
 
     ms_per_step = elapsed_ms / K
+    if shard_of:
+        total_params = my_params
     value = total_params / (ms_per_step * 1e-3)
     peak, peak_src = load_peaks()
     achieved = my_bytes / (step_ms_local * 1e-3) / 1e9
     roof = {"bound": "hbm", "kernel": "smo step (all launches of one step)", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
-            "algorithmic_bytes_per_launch": my_bytes, "traffic": load_traffic(wl.name, "step")}
+            "algorithmic_bytes_per_launch": my_bytes,
+            "traffic": load_traffic(wl.name, "step", shard_of or world, args.shard_rank if shard_of else rank)}
 
     # ---- ZeRO-1 completion: one in-place all-gather of the flat parameter buffer
     zero1 = None
@@ -643,8 +660,9 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32+int8", "data": "synthetic (seeded counter-hash N(0,0.02) params, N(0,1e-3) grads)",
-            "config": _config(wl, world),
-            "hbm_gbs": sum(costs) / (ms_per_step * 1e-3) / 1e9,
+            "config": dict(_config(wl, world), **({"shard": f"rank {args.shard_rank} of {shard_of}",
+                                                   "params": my_params} if shard_of else {})),
+            "hbm_gbs": (my_bytes if shard_of else sum(costs)) / (ms_per_step * 1e-3) / 1e9,
             "kernel_ms_per_step": step_ms,
             "roofline": roof,
             "cpu_baseline": cpu_ref or cpu,
