@@ -23,7 +23,7 @@
 extern "C" {
 #endif
 
-#define SMO_ABI_VERSION 2
+#define SMO_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define SMO_API __attribute__((visibility("default")))
@@ -49,6 +49,19 @@ typedef enum smo_kind {
     SMO_KIND_QUANT_ONLY = 4  /* full-resolution int8 moments (spatial_8bit.py:157-169) */
 } smo_kind;
 
+/* Element type of a tensor's param, grad, block scales and POOLED32 / DENSE
+ * moments (smo_tensor.dtype).  The reference computes in the parameter's
+ * dtype (spatial_8bit.py:118, :167, :195, :207): for BF16 / F16 every op is
+ * evaluated in fp32 and its result rounded to the dtype once, as torch's CPU
+ * kernels do; the alpha of add/add_ (weight decay, 1 - beta) is itself
+ * rounded to the dtype.  The int8 codes are int8 for every dtype.  Pointers of
+ * the float-typed fields below then point at 2-byte elements (cast them). */
+typedef enum smo_dtype {
+    SMO_DTYPE_F32 = 0,
+    SMO_DTYPE_BF16 = 1,
+    SMO_DTYPE_F16 = 2
+} smo_dtype;
+
 /* smo_tensor.flags */
 #define SMO_FLAG_GENERAL_PATH 1  /* step this tensor with the general two-launch kernels
                                     even when the fused single-pass kernel could take it */
@@ -72,10 +85,12 @@ typedef struct smo_hyper {
  * Fields a kind does not use must be NULL / 0.
  *
  *   POOLED8    param/grad [rows*cols]; codes [ceil(C/q_block)*q_block] int8,
- *              scales [ceil(C/q_block)] fp32, C = comp_rows*comp_cols
- *   POOLED32   param/grad [rows*cols]; m/v [comp_rows*comp_cols] fp32
- *   DENSE      param/grad/m/v [rows] fp32 (cols = 1)
- *   QUANT_ONLY param/grad [rows] fp32 (cols = 1); codes/scales as POOLED8 over rows
+ *              scales [ceil(C/q_block)], C = comp_rows*comp_cols
+ *   POOLED32   param/grad [rows*cols]; m/v [comp_rows*comp_cols]
+ *   DENSE      param/grad/m/v [rows] (cols = 1)
+ *   QUANT_ONLY param/grad [rows] (cols = 1); codes/scales as POOLED8 over rows
+ * Every non-code array holds elements of type `dtype` (fp32 for SMO_DTYPE_F32).
+ * Half-precision tensors take the general two-launch kernels.
  */
 typedef struct smo_tensor {
     float *param;
@@ -106,6 +121,8 @@ typedef struct smo_tensor {
        reconstructed moments are mapped back with the inverse permutations
        (row_perm_inv[row_perm[i]] = i).  All four null = no permutation. */
     const int64_t *row_perm, *col_perm, *row_perm_inv, *col_perm_inv;
+    int32_t dtype;                  /* smo_dtype (ABI 3) */
+    int32_t reserved;               /* 0 */
 } smo_tensor;
 
 /* ---- the optimizer step ------------------------------------------------ */

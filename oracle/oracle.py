@@ -32,8 +32,23 @@ class _Hyper(ctypes.Structure):
         ("beta2", ctypes.c_float), ("omb2", ctypes.c_float),
         ("wd", ctypes.c_float), ("wd_on", ctypes.c_int32),
         ("neg_step", ctypes.c_float), ("sqrt_bc2", ctypes.c_float),
-        ("eps", ctypes.c_float),
+        ("eps", ctypes.c_float), ("dtype", ctypes.c_int32),
     ]
+
+
+# parameter dtypes (the reference computes in the parameter's dtype)
+DTYPES = {"float32": 0, "bfloat16": 1, "float16": 2}
+
+
+def round_to(x: np.ndarray, dtype: str) -> np.ndarray:
+    """fp32 values rounded to ``dtype`` (nearest even) and widened back to fp32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if dtype == "bfloat16":
+        from smo_optimizer_b200 import synthetic
+        return synthetic.round_to_bf16(x)
+    if dtype == "float16":
+        return x.astype(np.float16).astype(np.float32)
+    return x
 
 
 def build(force: bool = False) -> str:
@@ -57,8 +72,8 @@ def lib():
         _lib.oracle_dense_step.argtypes = [P, P, P, P, i64, hp]
         _lib.oracle_quant_only_step.argtypes = [P, P, P, P, P, P, i64, i64, hp]
         _lib.oracle_pool_pair.argtypes = [P, P, i64, i64, i64, i64, hp, P, P]
-        _lib.oracle_quantize.argtypes = [P, i64, i64, P, P]
-        _lib.oracle_dequantize.argtypes = [P, P, i64, i64, P]
+        _lib.oracle_quantize_dt.argtypes = [P, i64, i64, P, P, ctypes.c_int]
+        _lib.oracle_dequantize_dt.argtypes = [P, P, i64, i64, P, ctypes.c_int]
         _lib.oracle_upsample.argtypes = [P, i64, i64, i64, i64, i64, P]
         _lib.oracle_num_threads.restype = ctypes.c_int
         _lib.oracle_set_num_threads.argtypes = [ctypes.c_int]
@@ -70,9 +85,9 @@ def _ptr(a: np.ndarray):
     return ctypes.c_void_p(a.ctypes.data)
 
 
-def hyper(s: _host.StepScalars) -> _Hyper:
+def hyper(s: _host.StepScalars, dtype: str = "float32") -> _Hyper:
     return _Hyper(float(s.beta1), float(s.omb1), float(s.beta2), float(s.omb2), float(s.wd),
-                  int(s.wd_on), float(s.neg_step), float(s.sqrt_bc2), float(s.eps))
+                  int(s.wd_on), float(s.neg_step), float(s.sqrt_bc2), float(s.eps), DTYPES[dtype])
 
 
 def num_threads() -> int:
@@ -85,19 +100,20 @@ def set_num_threads(n: int) -> None:
 
 # ---------------------------------------------------------------- primitives
 
-def quantize(x: np.ndarray, block: int):
-    """_quantize_blockwise (spatial_8bit.py:85-107): codes (nb, block), scales (nb, 1)."""
+def quantize(x: np.ndarray, block: int, dtype: str = "float32"):
+    """_quantize_blockwise (spatial_8bit.py:85-107): codes (nb, block), scales (nb, 1) in ``dtype``."""
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
     nb = _host.num_blocks(x.size, block)
     q = np.zeros((nb, block), np.int8)
     s = np.zeros((nb, 1), np.float32)
-    lib().oracle_quantize(_ptr(x), x.size, block, _ptr(q), _ptr(s))
+    lib().oracle_quantize_dt(_ptr(x), x.size, block, _ptr(q), _ptr(s), DTYPES[dtype])
     return q, s
 
 
-def dequantize(q: np.ndarray, s: np.ndarray, n: int, block: int) -> np.ndarray:
+def dequantize(q: np.ndarray, s: np.ndarray, n: int, block: int, dtype: str = "float32") -> np.ndarray:
     out = np.empty(n, np.float32)
-    lib().oracle_dequantize(_ptr(np.ascontiguousarray(q)), _ptr(np.ascontiguousarray(s)), n, block, _ptr(out))
+    lib().oracle_dequantize_dt(_ptr(np.ascontiguousarray(q)), _ptr(np.ascontiguousarray(s)), n, block, _ptr(out),
+                               DTYPES[dtype])
     return out
 
 
@@ -123,31 +139,31 @@ def upsample(src, out_shape, interp_band: int = 0):
 
 # ---------------------------------------------------------------- per-tensor steps
 
-def smo8bit_pooled_step(p2d, g2d, st, scalars, interp_band=0):
+def smo8bit_pooled_step(p2d, g2d, st, scalars, interp_band=0, dtype="float32"):
     H, W = p2d.shape
     h, w = st["comp_shape"]
     rc = lib().oracle_smo8bit_pooled_step(
         _ptr(p2d), _ptr(g2d), _ptr(st["m_q"]), _ptr(st["m_s"]), _ptr(st["v_q"]), _ptr(st["v_s"]),
-        H, W, h, w, st["q_block"], interp_band, ctypes.byref(hyper(scalars)))
+        H, W, h, w, st["q_block"], interp_band, ctypes.byref(hyper(scalars, dtype)))
     assert rc == 0, "oracle allocation failed"
 
 
-def smo_pooled_step(p2d, g2d, st, scalars):
+def smo_pooled_step(p2d, g2d, st, scalars, dtype="float32"):
     H, W = p2d.shape
     h, w = st["exp_avg"].shape
     rc = lib().oracle_smo_pooled_step(_ptr(p2d), _ptr(g2d), _ptr(st["exp_avg"]), _ptr(st["exp_avg_sq"]),
-                                      H, W, h, w, ctypes.byref(hyper(scalars)))
+                                      H, W, h, w, ctypes.byref(hyper(scalars, dtype)))
     assert rc == 0, "oracle allocation failed"
 
 
-def dense_step(p, g, st, scalars):
+def dense_step(p, g, st, scalars, dtype="float32"):
     lib().oracle_dense_step(_ptr(p), _ptr(g), _ptr(st["exp_avg"]), _ptr(st["exp_avg_sq"]), p.size,
-                            ctypes.byref(hyper(scalars)))
+                            ctypes.byref(hyper(scalars, dtype)))
 
 
-def quant_only_step(p, g, st, scalars):
+def quant_only_step(p, g, st, scalars, dtype="float32"):
     rc = lib().oracle_quant_only_step(_ptr(p), _ptr(g), _ptr(st["m_q"]), _ptr(st["m_s"]), _ptr(st["v_q"]),
-                                      _ptr(st["v_s"]), p.size, st["q_block"], ctypes.byref(hyper(scalars)))
+                                      _ptr(st["v_s"]), p.size, st["q_block"], ctypes.byref(hyper(scalars, dtype)))
     assert rc == 0, "oracle allocation failed"
 
 
@@ -159,11 +175,14 @@ class OracleOptimizer:
     ``groups`` is a list of dicts ``{"params": [np.ndarray, ...], ...}`` with
     optional per-group overrides and ``compress`` (True / False / "quant_only").
     Arrays are updated in place.  ``state`` is keyed by (group, index).
+    ``param_dtype`` ("float32", "bfloat16", "float16") is the dtype the
+    reference's parameters, gradients and state would have: arrays stay fp32
+    numpy arrays holding values of that dtype, and every op rounds to it.
     """
 
     def __init__(self, kind, groups, lr=1e-3, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.0,
                  k_ratio=0.25, block_size=64, low_peak=False, band_mb=64.0, compress_conv=False,
-                 permute_basis=False):
+                 permute_basis=False, param_dtype="float32"):
         assert kind in ("SMO8bit", "SMO")
         if low_peak and permute_basis:
             raise ValueError("permute_basis is not supported with low_peak")
@@ -179,6 +198,9 @@ class OracleOptimizer:
         self.band_mb = float(band_mb)
         self.compress_conv = bool(compress_conv)
         self.permute_basis = bool(permute_basis) and kind == "SMO8bit"
+        if param_dtype not in DTYPES:
+            raise ValueError(f"param_dtype must be one of {sorted(DTYPES)}")
+        self.dtype = param_dtype
         # permute_basis: (row_perm, col_perm) per state key, placed before the
         # first step (the reference draws them with torch.randperm,
         # spatial_8bit.py:202-204); absent keys get a seeded numpy permutation
@@ -200,8 +222,8 @@ class OracleOptimizer:
             st.update(is_quant_only=True, is_compressed=False, q_shape=tuple(p.shape), q_numel=p.size,
                       q_block=_host.quant_only_q_block(p.shape, group["block_size"]))
             z = np.zeros(p.size, np.float32)
-            st["m_q"], st["m_s"] = quantize(z, st["q_block"])
-            st["v_q"], st["v_s"] = quantize(z, st["q_block"])
+            st["m_q"], st["m_s"] = quantize(z, st["q_block"], self.dtype)
+            st["v_q"], st["v_s"] = quantize(z, st["q_block"], self.dtype)
             return st
         view = _host.compression_view(p.shape, self.compress_conv) if raw else None
         if view is not None:
@@ -212,8 +234,8 @@ class OracleOptimizer:
                 st["comp_numel"] = cs[0] * cs[1]
                 st["q_block"] = _host.pooled_q_block(pshape, cs, group["block_size"])
                 z = np.zeros(cs[0] * cs[1], np.float32)
-                st["m_q"], st["m_s"] = quantize(z, st["q_block"])
-                st["v_q"], st["v_s"] = quantize(z, st["q_block"])
+                st["m_q"], st["m_s"] = quantize(z, st["q_block"], self.dtype)
+                st["v_q"], st["v_s"] = quantize(z, st["q_block"], self.dtype)
                 st["comp_shape"] = cs
                 if self.permute_basis:
                     rp, cp = self.preset_perms.get(key) or (np.random.default_rng(0).permutation(vshape[0]),
@@ -241,27 +263,29 @@ class OracleOptimizer:
             sc = _host.step_scalars(group["lr"], group["betas"], group["eps"], group["weight_decay"],
                                     st["step"])
             g = np.ascontiguousarray(g, np.float32)
+            dt = self.dtype
             if st.get("is_quant_only"):
-                quant_only_step(p.reshape(-1), g.reshape(-1), st, sc)
+                quant_only_step(p.reshape(-1), g.reshape(-1), st, sc, dt)
             elif st["is_compressed"]:
                 p2 = p.reshape(st["orig_shape"])
                 g2 = g.reshape(st["orig_shape"])
                 if self.kind == "SMO8bit":
                     band = 0
                     if self.low_peak and _host.can_band(st["orig_shape"], st["comp_shape"]):
-                        band = _host.band_comp_rows(st["orig_shape"], st["comp_shape"], self.band_mb)
+                        band = _host.band_comp_rows(st["orig_shape"], st["comp_shape"], self.band_mb,
+                                                    4 if dt == "float32" else 2)
                     if "row_perm" in st:
                         # the step in the permuted basis (spatial_8bit.py:231-253): pool
                         # g[rp][:, cp], reconstruct there, map the update back
                         ix = np.ix_(st["row_perm"], st["col_perm"])
                         pp = np.ascontiguousarray(p2[ix])
-                        smo8bit_pooled_step(pp, np.ascontiguousarray(g2[ix]), st, sc, band)
+                        smo8bit_pooled_step(pp, np.ascontiguousarray(g2[ix]), st, sc, band, dt)
                         p2[ix] = pp
                     else:
-                        smo8bit_pooled_step(p2, g2, st, sc, band)
+                        smo8bit_pooled_step(p2, g2, st, sc, band, dt)
                 else:
-                    smo_pooled_step(p2, g2, st, sc)
+                    smo_pooled_step(p2, g2, st, sc, dt)
             else:
                 dense_step(p.reshape(-1), g.reshape(-1),
                            {"exp_avg": st["exp_avg"].reshape(-1), "exp_avg_sq": st["exp_avg_sq"].reshape(-1)},
-                           sc)
+                           sc, dt)

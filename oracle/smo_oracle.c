@@ -38,6 +38,16 @@
  * elements.  That touches only the parameter write (never the int8 codes) and
  * stays far inside the rtol 1e-5 parameter tolerance.
  *
+ * Half-precision parameters (bf16 / fp16, oracle_hyper.dtype): the reference
+ * then computes in the parameter's dtype (its state too: moments and block
+ * scales), and torch's CPU kernels for those dtypes evaluate every op in fp32
+ * exactly as above and round the op's result to the dtype once (rd()).  Two
+ * scalar rules were established against torch 2.11 CPU: the alpha of
+ * add/add_ (the weight decay and the EMA's 1-beta) is rounded to the dtype
+ * first; every other scalar (mul_, addcmul_'s value, addcdiv_'s value, the
+ * divisor and eps) stays fp32.  With dtype 0 (fp32) rd() is the identity and
+ * everything reduces to the sequence above.
+ *
  * Build with -ffp-contract=off: every fused multiply-add is written as fmaf.
  */
 #include <math.h>
@@ -57,7 +67,27 @@ typedef struct {
     float neg_step;         /* (float)(-(lr / (1 - beta1**step))) */
     float sqrt_bc2;         /* (float)sqrt(1 - beta2**step) */
     float eps;              /* (float)eps */
+    int32_t dtype;          /* parameter dtype: 0 fp32, 1 bf16, 2 fp16 */
 } oracle_hyper;
+
+/* fp32 -> bf16 / fp16 -> fp32, round to nearest even (the dtype's value as a float) */
+static inline float rd_bf16(float x)
+{
+    uint32_t u;
+    memcpy(&u, &x, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return x;           /* NaN */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    memcpy(&x, &u, 4);
+    return x;
+}
+
+static inline float rd(float x, int dtype)
+{
+    if (dtype == 1) return rd_bf16(x);
+    if (dtype == 2) return (float)(_Float16)x;
+    return x;
+}
 
 typedef struct {
     int64_t i0, i1;
@@ -141,7 +171,7 @@ static inline float interp_small(const float *src, int64_t w, coef_t rc, coef_t 
 
 static inline float decayed(float g, float p, const oracle_hyper *hp)
 {
-    return hp->wd_on ? fmaf(hp->wd, p, g) : g;
+    return hp->wd_on ? rd(fmaf(rd(hp->wd, hp->dtype), p, g), hp->dtype) : g;
 }
 
 /* _spatial_utils.py:72-91: stack(g, g*g) then avg_pool2d (exact) or
@@ -164,23 +194,24 @@ void oracle_pool_pair(const float *g, const float *p, int64_t H, int64_t W, int6
                 for (int64_t c = c0; c < c1; c++) {
                     float x = decayed(g[r * W + c], p[r * W + c], hp);
                     s1 = s1 + x;
-                    s2 = s2 + x * x;
+                    s2 = s2 + rd(x * x, hp->dtype);     /* torch.square, then the pool */
                 }
             if (exact) {
                 float div = (float)((r1 - r0) * (c1 - c0));
-                out_g[i * w + j] = s1 / div;
-                out_g2[i * w + j] = s2 / div;
+                out_g[i * w + j] = rd(s1 / div, hp->dtype);
+                out_g2[i * w + j] = rd(s2 / div, hp->dtype);
             } else {
                 float dh = (float)(r1 - r0), dw = (float)(c1 - c0);
-                out_g[i * w + j] = s1 / dh / dw;
-                out_g2[i * w + j] = s2 / dh / dw;
+                out_g[i * w + j] = rd(s1 / dh / dw, hp->dtype);
+                out_g2[i * w + j] = rd(s2 / dh / dw, hp->dtype);
             }
         }
     }
 }
 
-/* spatial_8bit.py:85-107.  q holds nb*B codes (the padded tail is coded too). */
-void oracle_quantize(const float *x, int64_t n, int64_t B, int8_t *q, float *s)
+/* spatial_8bit.py:85-107.  q holds nb*B codes (the padded tail is coded too);
+ * the scales are in the moments' dtype. */
+void oracle_quantize_dt(const float *x, int64_t n, int64_t B, int8_t *q, float *s, int dtype)
 {
     int64_t nb = (n + B - 1) / B;
 #pragma omp parallel for schedule(static)
@@ -192,12 +223,12 @@ void oracle_quantize(const float *x, int64_t n, int64_t B, int8_t *q, float *s)
             if (a > m || a != a) m = a;
             if (m != m) break;
         }
-        float sc = (m < 1e-12f) ? 1e-12f : m;
+        float sc = rd((m < 1e-12f) ? 1e-12f : m, dtype);
         s[b] = sc;
         for (int64_t k = 0; k < B; k++) {
             int64_t i = b * B + k;
             float v = i < n ? x[i] : 0.0f;
-            float r = rintf((v / sc) * 127.0f);
+            float r = rintf(rd(rd(v / sc, dtype) * 127.0f, dtype));
             if (r == 0.0f && v != 0.0f && v == v) r = v > 0.0f ? 1.0f : -1.0f;
             if (r > 127.0f) r = 127.0f;
             if (r < -127.0f) r = -127.0f;
@@ -206,14 +237,24 @@ void oracle_quantize(const float *x, int64_t n, int64_t B, int8_t *q, float *s)
     }
 }
 
-/* spatial_8bit.py:109-122 */
-void oracle_dequantize(const int8_t *q, const float *s, int64_t n, int64_t B, float *out)
+void oracle_quantize(const float *x, int64_t n, int64_t B, int8_t *q, float *s)
+{
+    oracle_quantize_dt(x, n, B, q, s, 0);
+}
+
+/* spatial_8bit.py:109-122 (dequantised to the moments' dtype) */
+void oracle_dequantize_dt(const int8_t *q, const float *s, int64_t n, int64_t B, float *out, int dtype)
 {
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
-        float t = s[i / B] / 127.0f;
-        out[i] = (float)q[i] * t;
+        float t = rd(s[i / B] / 127.0f, dtype);
+        out[i] = rd((float)q[i] * t, dtype);
     }
+}
+
+void oracle_dequantize(const int8_t *q, const float *s, int64_t n, int64_t B, float *out)
+{
+    oracle_dequantize_dt(q, s, n, B, out, 0);
 }
 
 /* _spatial_utils.py:128-176 (one channel), with the low_peak band emulation. */
@@ -237,9 +278,10 @@ void oracle_upsample(const float *src, int64_t h, int64_t w, int64_t H, int64_t 
 /* the shared Adam write (spatial_8bit.py:289-297, :369-370; spatial.py:192-206) */
 static inline float adam_write(float p, float mh, float vh, const oracle_hyper *hp)
 {
-    float d = sqrtf(vh) / hp->sqrt_bc2 + hp->eps;
+    const int dt = hp->dtype;
+    float d = rd(rd(rd(sqrtf(vh), dt) / hp->sqrt_bc2, dt) + hp->eps, dt);
     float u = (hp->neg_step * mh) / d;
-    return p + u;
+    return rd(p + u, dt);
 }
 
 /* EMA of the compact moments and the parameter write for a pooled tensor whose
@@ -266,6 +308,8 @@ static void pooled_write(float *p, const float *m, const float *v, int64_t H, in
                     mh = interp_generic(m, w, rc, cc, r, q);
                     vh = interp_generic(v, w, rc, cc, r, q);
                 }
+                mh = rd(mh, hp->dtype);
+                vh = rd(vh, hp->dtype);
             }
             if (vh < 0.0f) vh = 0.0f;           /* clamp(min=0), NaN passes through */
             p[r * W + q] = adam_write(p[r * W + q], mh, vh, hp);
@@ -288,16 +332,17 @@ int oracle_smo8bit_pooled_step(float *p, const float *g, int8_t *mq, float *ms, 
     float *gm = malloc(sizeof(float) * C), *g2 = malloc(sizeof(float) * C);
     float *m = malloc(sizeof(float) * C), *v = malloc(sizeof(float) * C);
     if (!gm || !g2 || !m || !v) { free(gm); free(g2); free(m); free(v); return 1; }
+    const int dt = hp->dtype;
     oracle_pool_pair(g, p, H, W, h, w, hp, gm, g2);
-    oracle_dequantize(mq, ms, C, B, m);
-    oracle_dequantize(vq, vs, C, B, v);
+    oracle_dequantize_dt(mq, ms, C, B, m, dt);
+    oracle_dequantize_dt(vq, vs, C, B, v, dt);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < C; i++) {
-        m[i] = fmaf(hp->omb1, gm[i], m[i] * hp->beta1);
-        v[i] = fmaf(hp->omb2, g2[i], v[i] * hp->beta2);
+        m[i] = rd(fmaf(rd(hp->omb1, dt), gm[i], rd(m[i] * hp->beta1, dt)), dt);
+        v[i] = rd(fmaf(rd(hp->omb2, dt), g2[i], rd(v[i] * hp->beta2, dt)), dt);
     }
-    oracle_quantize(m, C, B, mq, ms);
-    oracle_quantize(v, C, B, vq, vs);
+    oracle_quantize_dt(m, C, B, mq, ms, dt);
+    oracle_quantize_dt(v, C, B, vq, vs, dt);
     pooled_write(p, m, v, H, W, h, w, interp_band, hp);
     free(gm); free(g2); free(m); free(v);
     return 0;
@@ -310,11 +355,12 @@ int oracle_smo_pooled_step(float *p, const float *g, float *m, float *v,
     int64_t C = h * w;
     float *gm = malloc(sizeof(float) * C), *g2 = malloc(sizeof(float) * C);
     if (!gm || !g2) { free(gm); free(g2); return 1; }
+    const int dt = hp->dtype;
     oracle_pool_pair(g, p, H, W, h, w, hp, gm, g2);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < C; i++) {
-        m[i] = fmaf(hp->omb1, gm[i], m[i] * hp->beta1);
-        v[i] = fmaf(hp->omb2, g2[i], v[i] * hp->beta2);
+        m[i] = rd(fmaf(rd(hp->omb1, dt), gm[i], rd(m[i] * hp->beta1, dt)), dt);
+        v[i] = rd(fmaf(rd(hp->omb2, dt), g2[i], rd(v[i] * hp->beta2, dt)), dt);
     }
     pooled_write(p, m, v, H, W, h, w, 0, hp);
     free(gm); free(g2);
@@ -324,11 +370,12 @@ int oracle_smo_pooled_step(float *p, const float *g, float *m, float *v,
 /* dense Adam moments (spatial_8bit.py:278-283, spatial.py:184-189) */
 void oracle_dense_step(float *p, const float *g, float *m, float *v, int64_t n, const oracle_hyper *hp)
 {
+    const int dt = hp->dtype;
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         float x = decayed(g[i], p[i], hp);
-        m[i] = fmaf(hp->omb1, x, m[i] * hp->beta1);
-        v[i] = fmaf(hp->omb2 * x, x, v[i] * hp->beta2);
+        m[i] = rd(fmaf(rd(hp->omb1, dt), x, rd(m[i] * hp->beta1, dt)), dt);   /* add_(alpha): dtype alpha */
+        v[i] = rd(fmaf(hp->omb2 * x, x, rd(v[i] * hp->beta2, dt)), dt);       /* addcmul_(value): fp32 value */
         p[i] = adam_write(p[i], m[i], v[i], hp);
     }
 }
@@ -339,16 +386,17 @@ int oracle_quant_only_step(float *p, const float *g, int8_t *mq, float *ms, int8
 {
     float *m = malloc(sizeof(float) * n), *v = malloc(sizeof(float) * n);
     if (!m || !v) { free(m); free(v); return 1; }
-    oracle_dequantize(mq, ms, n, B, m);
-    oracle_dequantize(vq, vs, n, B, v);
+    const int dt = hp->dtype;
+    oracle_dequantize_dt(mq, ms, n, B, m, dt);
+    oracle_dequantize_dt(vq, vs, n, B, v, dt);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++) {
         float x = decayed(g[i], p[i], hp);
-        m[i] = fmaf(hp->omb1, x, m[i] * hp->beta1);
-        v[i] = fmaf(hp->omb2 * x, x, v[i] * hp->beta2);
+        m[i] = rd(fmaf(rd(hp->omb1, dt), x, rd(m[i] * hp->beta1, dt)), dt);
+        v[i] = rd(fmaf(hp->omb2 * x, x, rd(v[i] * hp->beta2, dt)), dt);
     }
-    oracle_quantize(m, n, B, mq, ms);
-    oracle_quantize(v, n, B, vq, vs);
+    oracle_quantize_dt(m, n, B, mq, ms, dt);
+    oracle_quantize_dt(v, n, B, vq, vs, dt);
 #pragma omp parallel for schedule(static)
     for (int64_t i = 0; i < n; i++)
         p[i] = adam_write(p[i], m[i], v[i], hp);

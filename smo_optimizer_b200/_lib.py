@@ -19,7 +19,10 @@ SMO_KIND_POOLED32 = 2
 SMO_KIND_DENSE = 3
 SMO_KIND_QUANT_ONLY = 4
 SMO_ERR_TIMEOUT = 5
-ABI_VERSION = 2
+SMO_DTYPE_F32 = 0
+SMO_DTYPE_BF16 = 1
+SMO_DTYPE_F16 = 2
+ABI_VERSION = 3
 
 # Field layout of struct smo_hyper / smo_tensor, as a numpy structured dtype so
 # that descriptor tables are filled column-wise without per-field Python calls.
@@ -39,6 +42,7 @@ TENSOR_DTYPE = np.dtype([
     ("kind", np.int32), ("flags", np.int32),
     ("hp", HYPER_DTYPE),
     ("row_perm", np.uint64), ("col_perm", np.uint64), ("row_perm_inv", np.uint64), ("col_perm_inv", np.uint64),
+    ("dtype", np.int32), ("reserved", np.int32),
 ])
 
 HYPER_FIELDS = HYPER_DTYPE.names

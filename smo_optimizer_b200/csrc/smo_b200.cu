@@ -15,6 +15,8 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "smo_common.cuh"
@@ -43,16 +45,21 @@ __device__ __forceinline__ int find_tensor(const int64_t *start, int n, int64_t 
     return lo;
 }
 
+// Storage type T of param, grad, block scales and fp32-kind moments (float,
+// __nv_bfloat16, __half); the post-EMA scratch of POOLED8 is fp32 (its values
+// are already rounded to T).  rd<T> rounds each op to T (identity for float).
+template <class T>
 __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t C = d.h * d.w;
     const bool q8 = (d.kind == SMO_KIND_POOLED8);
     const int64_t BI = q8 ? d.B : kPooled32Chunk;
     const int64_t base = item * BI;
     const smo_hyper &hp = d.hp;
+    const T *g = (const T *)d.g, *p = (const T *)d.p;
     float tm = 0.0f, tv = 0.0f;
     if (q8) {
-        tm = dequant_step(d.ms_in[item]);
-        tv = dequant_step(d.vs_in[item]);
+        tm = dequant_step<T>(ld<T>((const T *)d.ms_in + item));
+        tv = dequant_step<T>(ld<T>((const T *)d.vs_in + item));
     }
     float am = 0.0f, av = 0.0f;
     for (int64_t k = lane; k < BI; k += 32) {
@@ -60,25 +67,30 @@ __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
         if (c >= C) break;
         int64_t i = c / d.w, j = c - i * d.w;
         float gm, g2;
-        pool_cell(d.g, d.p, d.H, d.W, d.h, d.w, d.exact, i, j, hp, gm, g2, d.rp, d.cp);
+        pool_cell<T>(g, p, d.H, d.W, d.h, d.w, d.exact, i, j, hp, gm, g2, d.rp, d.cp);
         float m, v;
         if (q8) {
-            m = dequant1(d.mq_in[c], tm);
-            v = dequant1(d.vq_in[c], tv);
+            m = dequant1<T>(d.mq_in[c], tm);
+            v = dequant1<T>(d.vq_in[c], tv);
         } else {
-            m = d.m_in[c];
-            v = d.v_in[c];
+            m = ld<T>((const T *)d.m_in + c);
+            v = ld<T>((const T *)d.v_in + c);
         }
-        m = ema(m, gm, hp.beta1, hp.omb1);
-        v = ema(v, g2, hp.beta2, hp.omb2);
-        d.m_out[c] = m;
-        d.v_out[c] = v;
+        m = ema<T>(m, gm, hp.beta1, hp.omb1);
+        v = ema<T>(v, g2, hp.beta2, hp.omb2);
+        if (q8) {
+            d.m_out[c] = m;
+            d.v_out[c] = v;
+        } else {
+            st<T>((T *)d.m_out + c, m);
+            st<T>((T *)d.v_out + c, v);
+        }
         am = absmax_acc(am, m);
         av = absmax_acc(av, v);
     }
     if (!q8) return;
-    const float sm = block_scale(warp_absmax(am));
-    const float sv = block_scale(warp_absmax(av));
+    const float sm = block_scale<T>(warp_absmax(am));
+    const float sv = block_scale<T>(warp_absmax(av));
     for (int64_t k = lane; k < BI; k += 32) {
         int64_t c = base + k;
         float m = 0.0f, v = 0.0f;
@@ -86,71 +98,78 @@ __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
             m = d.m_out[c];
             v = d.v_out[c];
         }
-        d.mq_out[c] = quantize1(m, sm);
-        d.vq_out[c] = quantize1(v, sv);
+        d.mq_out[c] = quantize1<T>(m, sm);
+        d.vq_out[c] = quantize1<T>(v, sv);
     }
     if (lane == 0) {
-        d.ms_out[item] = sm;
-        d.vs_out[item] = sv;
+        st<T>((T *)d.ms_out + item, sm);
+        st<T>((T *)d.vs_out + item, sv);
     }
 }
 
+template <class T>
 __device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t N = d.H;
     const int64_t B = d.B;
     const int64_t base = item * B;
     const smo_hyper &hp = d.hp;
-    const float tm = dequant_step(d.ms_in[item]);
-    const float tv = dequant_step(d.vs_in[item]);
+    const T *g = (const T *)d.g;
+    T *p = (T *)d.p;
+    const float tm = dequant_step<T>(ld<T>((const T *)d.ms_in + item));
+    const float tv = dequant_step<T>(ld<T>((const T *)d.vs_in + item));
     float am = 0.0f, av = 0.0f;
     for (int64_t k = lane; k < B; k += 32) {
         int64_t i = base + k;
         if (i >= N) break;
-        float x = decayed(d.g[i], d.p[i], hp);
-        float m = ema(dequant1(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
-        float v = ema_sq(dequant1(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
+        float x = decayed<T>(ld<T>(g + i), ld<T>(p + i), hp);
+        float m = ema<T>(dequant1<T>(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
+        float v = ema_sq<T>(dequant1<T>(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
         am = absmax_acc(am, m);
         av = absmax_acc(av, v);
     }
-    const float sm = block_scale(warp_absmax(am));
-    const float sv = block_scale(warp_absmax(av));
+    const float sm = block_scale<T>(warp_absmax(am));
+    const float sv = block_scale<T>(warp_absmax(av));
     for (int64_t k = lane; k < B; k += 32) {
         int64_t i = base + k;
         if (i < N) {
-            float p = d.p[i];
-            float x = decayed(d.g[i], p, hp);
-            float m = ema(dequant1(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
-            float v = ema_sq(dequant1(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
-            d.mq_out[i] = quantize1(m, sm);
-            d.vq_out[i] = quantize1(v, sv);
-            d.p[i] = adam_write(p, m, v, hp);
+            float pi = ld<T>(p + i);
+            float x = decayed<T>(ld<T>(g + i), pi, hp);
+            float m = ema<T>(dequant1<T>(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
+            float v = ema_sq<T>(dequant1<T>(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
+            d.mq_out[i] = quantize1<T>(m, sm);
+            d.vq_out[i] = quantize1<T>(v, sv);
+            st<T>(p + i, adam_write<T>(pi, m, v, hp));
         } else {
             d.mq_out[i] = 0;
             d.vq_out[i] = 0;
         }
     }
     if (lane == 0) {
-        d.ms_out[item] = sm;
-        d.vs_out[item] = sv;
+        st<T>((T *)d.ms_out + item, sm);
+        st<T>((T *)d.vs_out + item, sv);
     }
 }
 
+template <class T>
 __device__ void dense_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t N = d.H;
     const int64_t base = item * kDenseChunk;
     const int64_t end = base + kDenseChunk < N ? base + kDenseChunk : N;
     const smo_hyper &hp = d.hp;
+    const T *g = (const T *)d.g, *m_in = (const T *)d.m_in, *v_in = (const T *)d.v_in;
+    T *p = (T *)d.p, *m_out = (T *)d.m_out, *v_out = (T *)d.v_out;
     for (int64_t i = base + lane; i < end; i += 32) {
-        float p = d.p[i];
-        float x = decayed(d.g[i], p, hp);
-        float m = ema(d.m_in[i], x, hp.beta1, hp.omb1);
-        float v = ema_sq(d.v_in[i], x, hp.beta2, hp.omb2);
-        d.m_out[i] = m;
-        d.v_out[i] = v;
-        d.p[i] = adam_write(p, m, v, hp);
+        float pi = ld<T>(p + i);
+        float x = decayed<T>(ld<T>(g + i), pi, hp);
+        float m = ema<T>(ld<T>(m_in + i), x, hp.beta1, hp.omb1);
+        float v = ema_sq<T>(ld<T>(v_in + i), x, hp.beta2, hp.omb2);
+        st<T>(m_out + i, m);
+        st<T>(v_out + i, v);
+        st<T>(p + i, adam_write<T>(pi, m, v, hp));
     }
 }
 
+template <class T>
 __global__ void __launch_bounds__(256) step_a_kernel(const __grid_constant__ Batch b) {
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -162,14 +181,48 @@ __global__ void __launch_bounds__(256) step_a_kernel(const __grid_constant__ Bat
         const int64_t item = it - b.start_a[t];
         switch (d.kind) {
             case SMO_KIND_POOLED8:
-            case SMO_KIND_POOLED32: pooled_block_item(d, item, lane); break;
-            case SMO_KIND_QUANT_ONLY: quant_only_item(d, item, lane); break;
-            case SMO_KIND_DENSE: dense_item(d, item, lane); break;
+            case SMO_KIND_POOLED32: pooled_block_item<T>(d, item, lane); break;
+            case SMO_KIND_QUANT_ONLY: quant_only_item<T>(d, item, lane); break;
+            case SMO_KIND_DENSE: dense_item<T>(d, item, lane); break;
             default: break;
         }
     }
 }
 
+// One full-resolution row r of a pooled tensor: moments of type S (fp32
+// scratch for POOLED8, the state's type T for POOLED32), parameter of type T.
+template <class T, class S>
+__device__ __forceinline__ void adam_row(const DevDesc &d, int64_t r, int lane) {
+    const S *mo = (const S *)d.m_out, *vo = (const S *)d.v_out;
+    // permute_basis: parameter row r / column q sit at row rpi[r] / column
+    // cpi[q] of the basis the moments were reconstructed in
+    const int64_t br = d.rpi ? d.rpi[r] : r;
+    int small;
+    const Coef rc = row_coef(br, d.H, d.h, d.W, d.band, small);
+    T *prow = (T *)d.p + r * d.W;
+    for (int64_t q = lane; q < d.W; q += 32) {
+        const int64_t bq = d.cpi ? d.cpi[q] : q;
+        float mh, vh;
+        if (d.same) {
+            mh = ld<S>(mo + br * d.w + bq);
+            vh = ld<S>(vo + br * d.w + bq);
+        } else {
+            const Coef cc = coef_for(bq, d.w, d.W);
+            if (small) {
+                mh = interp_small<S>(mo, d.w, rc, cc);
+                vh = interp_small<S>(vo, d.w, rc, cc);
+            } else {
+                mh = interp_generic<S>(mo, d.w, rc, cc, br, bq);
+                vh = interp_generic<S>(vo, d.w, rc, cc, br, bq);
+            }
+            mh = rd<T>(mh);
+            vh = rd<T>(vh);
+        }
+        st<T>(prow + q, adam_write<T>(ld<T>(prow + q), mh, clamp_min0(vh), d.hp));
+    }
+}
+
+template <class T>
 __global__ void __launch_bounds__(256) step_b_kernel(const __grid_constant__ Batch b) {
     const int lane = threadIdx.x & 31;
     const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -179,30 +232,8 @@ __global__ void __launch_bounds__(256) step_b_kernel(const __grid_constant__ Bat
         const int t = find_tensor(b.start_b, b.n, it);
         const DevDesc &d = b.d[t];
         const int64_t r = it - b.start_b[t];
-        // permute_basis: parameter row r / column q sit at row rpi[r] / column
-        // cpi[q] of the basis the moments were reconstructed in
-        const int64_t br = d.rpi ? d.rpi[r] : r;
-        int small;
-        const Coef rc = row_coef(br, d.H, d.h, d.W, d.band, small);
-        float *prow = d.p + r * d.W;
-        for (int64_t q = lane; q < d.W; q += 32) {
-            const int64_t bq = d.cpi ? d.cpi[q] : q;
-            float mh, vh;
-            if (d.same) {
-                mh = d.m_out[br * d.w + bq];
-                vh = d.v_out[br * d.w + bq];
-            } else {
-                const Coef cc = coef_for(bq, d.w, d.W);
-                if (small) {
-                    mh = interp_small(d.m_out, d.w, rc, cc);
-                    vh = interp_small(d.v_out, d.w, rc, cc);
-                } else {
-                    mh = interp_generic(d.m_out, d.w, rc, cc, br, bq);
-                    vh = interp_generic(d.v_out, d.w, rc, cc, br, bq);
-                }
-            }
-            prow[q] = adam_write(prow[q], mh, clamp_min0(vh), d.hp);
-        }
+        if (d.kind == SMO_KIND_POOLED32) adam_row<T, T>(d, r, lane);
+        else adam_row<T, float>(d, r, lane);
     }
 }
 
@@ -360,13 +391,17 @@ static inline bool aligned(const void *ptr, size_t a) { return ((uintptr_t)ptr %
 static int make_desc(const smo_tensor &t, DevDesc &d) {
     memset(&d, 0, sizeof(d));
     if (!t.param || !t.grad) return SMO_ERR_INVALID;
-    if (!aligned(t.param, 4) || !aligned(t.grad, 4)) return SMO_ERR_ALIGNMENT;
+    if (t.dtype != SMO_DTYPE_F32 && t.dtype != SMO_DTYPE_BF16 && t.dtype != SMO_DTYPE_F16) return SMO_ERR_INVALID;
+    // element size of param, grad, scales and fp32-kind moments
+    const size_t es = t.dtype == SMO_DTYPE_F32 ? 4 : 2;
+    if (!aligned(t.param, es) || !aligned(t.grad, es)) return SMO_ERR_ALIGNMENT;
     const int nperm = (t.row_perm != nullptr) + (t.col_perm != nullptr) + (t.row_perm_inv != nullptr) +
                       (t.col_perm_inv != nullptr);
     if (nperm && t.kind != SMO_KIND_POOLED8 && t.kind != SMO_KIND_POOLED32) return SMO_ERR_INVALID;
     d.p = t.param;
     d.g = t.grad;
     d.kind = t.kind;
+    d.dtype = t.dtype;
     d.hp = t.hp;
     d.H = t.rows;
     d.W = t.cols;
@@ -398,15 +433,15 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
                 if (!t.m_q_in || !t.m_s_in || !t.v_q_in || !t.v_s_in || !t.m_q_out || !t.m_s_out || !t.v_q_out ||
                     !t.v_s_out)
                     return SMO_ERR_INVALID;
-                if (!aligned(t.m_s_in, 4) || !aligned(t.v_s_in, 4) || !aligned(t.m_s_out, 4) ||
-                    !aligned(t.v_s_out, 4))
+                if (!aligned(t.m_s_in, es) || !aligned(t.v_s_in, es) || !aligned(t.m_s_out, es) ||
+                    !aligned(t.v_s_out, es))
                     return SMO_ERR_ALIGNMENT;
                 d.B = t.q_block;
                 d.mq_in = t.m_q_in; d.ms_in = t.m_s_in; d.vq_in = t.v_q_in; d.vs_in = t.v_s_in;
                 d.mq_out = t.m_q_out; d.ms_out = t.m_s_out; d.vq_out = t.v_q_out; d.vs_out = t.v_s_out;
             } else {
                 if (!t.m_in || !t.v_in || !t.m_out || !t.v_out) return SMO_ERR_INVALID;
-                if (!aligned(t.m_in, 4) || !aligned(t.v_in, 4) || !aligned(t.m_out, 4) || !aligned(t.v_out, 4))
+                if (!aligned(t.m_in, es) || !aligned(t.v_in, es) || !aligned(t.m_out, es) || !aligned(t.v_out, es))
                     return SMO_ERR_ALIGNMENT;
                 d.m_in = t.m_in; d.v_in = t.v_in; d.m_out = t.m_out; d.v_out = t.v_out;
             }
@@ -415,7 +450,7 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
         case SMO_KIND_DENSE:
             if (t.rows < 0 || t.cols != 1) return SMO_ERR_INVALID;
             if (!t.m_in || !t.v_in || !t.m_out || !t.v_out) return SMO_ERR_INVALID;
-            if (!aligned(t.m_in, 4) || !aligned(t.v_in, 4) || !aligned(t.m_out, 4) || !aligned(t.v_out, 4))
+            if (!aligned(t.m_in, es) || !aligned(t.v_in, es) || !aligned(t.m_out, es) || !aligned(t.v_out, es))
                 return SMO_ERR_ALIGNMENT;
             d.m_in = t.m_in; d.v_in = t.v_in; d.m_out = t.m_out; d.v_out = t.v_out;
             return SMO_OK;
@@ -424,7 +459,7 @@ static int make_desc(const smo_tensor &t, DevDesc &d) {
             if (!t.m_q_in || !t.m_s_in || !t.v_q_in || !t.v_s_in || !t.m_q_out || !t.m_s_out || !t.v_q_out ||
                 !t.v_s_out)
                 return SMO_ERR_INVALID;
-            if (!aligned(t.m_s_in, 4) || !aligned(t.v_s_in, 4) || !aligned(t.m_s_out, 4) || !aligned(t.v_s_out, 4))
+            if (!aligned(t.m_s_in, es) || !aligned(t.v_s_in, es) || !aligned(t.m_s_out, es) || !aligned(t.v_s_out, es))
                 return SMO_ERR_ALIGNMENT;
             d.B = t.q_block;
             d.mq_in = t.m_q_in; d.ms_in = t.m_s_in; d.vq_in = t.v_q_in; d.vs_in = t.v_s_in;
@@ -467,7 +502,8 @@ static inline size_t general_scratch(const smo_tensor &t) {
     return 2 * round_up((size_t)t.comp_rows * (size_t)t.comp_cols * sizeof(float), kScratchAlign);
 }
 
-static int launch_general(Batch &b, cudaStream_t stream) {
+template <class T>
+static int launch_general_t(Batch &b, cudaStream_t stream) {
     b.start_a[0] = 0;
     b.start_b[0] = 0;
     for (int i = 0; i < b.n; i++) {
@@ -479,7 +515,7 @@ static int launch_general(Batch &b, cudaStream_t stream) {
     if (b.start_a[b.n] > 0) {
         int64_t blocks = (b.start_a[b.n] + warps - 1) / warps;
         blocks = blocks < cap ? blocks : cap;
-        step_a_kernel<<<(unsigned)blocks, threads, 0, stream>>>(b);
+        step_a_kernel<T><<<(unsigned)blocks, threads, 0, stream>>>(b);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(e);
         g_launches++;
@@ -487,12 +523,20 @@ static int launch_general(Batch &b, cudaStream_t stream) {
     if (b.start_b[b.n] > 0) {
         int64_t blocks = (b.start_b[b.n] + warps - 1) / warps;
         blocks = blocks < cap ? blocks : cap;
-        step_b_kernel<<<(unsigned)blocks, threads, 0, stream>>>(b);
+        step_b_kernel<T><<<(unsigned)blocks, threads, 0, stream>>>(b);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return cuda_fail(e);
         g_launches++;
     }
     return SMO_OK;
+}
+
+static int launch_general(Batch &b, int32_t dtype, cudaStream_t stream) {
+    switch (dtype) {
+        case SMO_DTYPE_BF16: return launch_general_t<__nv_bfloat16>(b, stream);
+        case SMO_DTYPE_F16: return launch_general_t<__half>(b, stream);
+        default: return launch_general_t<float>(b, stream);
+    }
 }
 
 }  // namespace smo
@@ -527,31 +571,36 @@ int smo_step(const smo_tensor *tensors, int32_t n, void *workspace, size_t works
     st = fused_step(tensors, n, ws, flag_bytes, stream);
     if (st != SMO_OK) return st;
 
-    // Everything else goes through the general two-launch path, batched; its
-    // scratch starts after the fused kernel's flag words.
+    // Everything else goes through the general two-launch path, batched by
+    // storage type; its scratch starts after the fused kernel's flag words.
     static thread_local Batch batch;
     const size_t base = kWsHeader + flag_bytes;
-    size_t off = base;
-    batch.n = 0;
-    for (int32_t i = 0; i < n; i++) {
-        if (fused_takes(tensors[i])) continue;
-        DevDesc &d = batch.d[batch.n];
-        make_desc(tensors[i], d);
-        if (d.kind == SMO_KIND_POOLED8) {
-            const size_t bytes = round_up((size_t)(d.h * d.w) * sizeof(float), kScratchAlign);
-            d.m_out = (float *)(ws + off);
-            d.v_out = (float *)(ws + off + bytes);
-            off += 2 * bytes;
+    for (int32_t dt = SMO_DTYPE_F32; dt <= SMO_DTYPE_F16; dt++) {
+        size_t off = base;
+        batch.n = 0;
+        for (int32_t i = 0; i < n; i++) {
+            if (tensors[i].dtype != dt || fused_takes(tensors[i])) continue;
+            DevDesc &d = batch.d[batch.n];
+            make_desc(tensors[i], d);
+            if (d.kind == SMO_KIND_POOLED8) {
+                const size_t bytes = round_up((size_t)(d.h * d.w) * sizeof(float), kScratchAlign);
+                d.m_out = (float *)(ws + off);
+                d.v_out = (float *)(ws + off + bytes);
+                off += 2 * bytes;
+            }
+            batch.n++;
+            if (batch.n == kMaxBatch) {
+                st = launch_general(batch, dt, stream);
+                if (st != SMO_OK) return st;
+                batch.n = 0;
+                off = base;  // stream order: the next launch pair starts after this one ends
+            }
         }
-        batch.n++;
-        if (batch.n == kMaxBatch) {
-            st = launch_general(batch, stream);
+        if (batch.n > 0) {
+            st = launch_general(batch, dt, stream);
             if (st != SMO_OK) return st;
-            batch.n = 0;
-            off = base;  // stream order: the next launch pair starts after this one ends
         }
     }
-    if (batch.n > 0) return launch_general(batch, stream);
     return SMO_OK;
 }
 

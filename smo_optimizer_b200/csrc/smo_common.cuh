@@ -5,37 +5,73 @@
 // __fmaf_rn where torch fuses a multiply-add, __fmul_rn / __fadd_rn /
 // __fdiv_rn / __fsqrt_rn where it rounds each operation.  The library is also
 // compiled with -fmad=false so that nothing else is contracted.
+//
+// The storage type T of a tensor (float, __nv_bfloat16, __half) is a template
+// parameter: for half-precision parameters the reference computes in the
+// parameter's dtype, and torch's CPU kernels evaluate each op in fp32 and
+// round its result to the dtype once, which rd<T>() does at each op boundary
+// (the identity for float).  The alpha of add/add_ (weight decay, the EMA's
+// 1 - beta) is itself rounded to the dtype; other scalars stay fp32.
 #pragma once
 
 #include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "smo_b200.h"
 
 namespace smo {
 
+// ---------------------------------------------------------------- storage types
+
+template <class T>
+__device__ __forceinline__ float rd(float x) { return x; }
+template <>
+__device__ __forceinline__ float rd<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+template <>
+__device__ __forceinline__ float rd<__half>(float x) { return __half2float(__float2half_rn(x)); }
+
+template <class T>
+__device__ __forceinline__ float ld(const T *p) { return *p; }
+template <>
+__device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16 *p) { return __bfloat162float(*p); }
+template <>
+__device__ __forceinline__ float ld<__half>(const __half *p) { return __half2float(*p); }
+
+template <class T>
+__device__ __forceinline__ void st(T *p, float x) { *p = x; }
+template <>
+__device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16 *p, float x) { *p = __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ void st<__half>(__half *p, float x) { *p = __float2half_rn(x); }
+
 // ---------------------------------------------------------------- scalars
 
 // x = g + wd * p  (grad.add(p, alpha=wd), spatial_8bit.py:217-218)
+template <class T = float>
 __device__ __forceinline__ float decayed(float g, float p, const smo_hyper &hp) {
-    return hp.wd_on ? __fmaf_rn(hp.weight_decay, p, g) : g;
+    return hp.wd_on ? rd<T>(__fmaf_rn(rd<T>(hp.weight_decay), p, g)) : g;
 }
 
 // m.mul_(b1).add_(u, alpha=1-b1)  (spatial_8bit.py:240-242)
+template <class T = float>
 __device__ __forceinline__ float ema(float m, float u, float beta, float omb) {
-    return __fmaf_rn(omb, u, __fmul_rn(m, beta));
+    return rd<T>(__fmaf_rn(rd<T>(omb), u, rd<T>(__fmul_rn(m, beta))));
 }
 
 // v.mul_(b2).addcmul_(x, x, value=1-b2)  (spatial_8bit.py:281)
+template <class T = float>
 __device__ __forceinline__ float ema_sq(float v, float x, float beta, float omb) {
-    return __fmaf_rn(__fmul_rn(omb, x), x, __fmul_rn(v, beta));
+    return rd<T>(__fmaf_rn(__fmul_rn(omb, x), x, rd<T>(__fmul_rn(v, beta))));
 }
 
 // denom = sqrt(v)/sqrt(bc2) + eps;  p.addcdiv_(m, denom, value=-step_size)
 // (spatial_8bit.py:293-297)
+template <class T = float>
 __device__ __forceinline__ float adam_write(float p, float m, float v, const smo_hyper &hp) {
-    float d = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), hp.sqrt_bc2), hp.eps);
-    return __fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d));
+    float d = rd<T>(__fadd_rn(rd<T>(__fdiv_rn(rd<T>(__fsqrt_rn(v)), hp.sqrt_bc2)), hp.eps));
+    return rd<T>(__fadd_rn(p, __fdiv_rn(__fmul_rn(hp.neg_step, m), d)));
 }
 
 // ---------------------------------------------------------------- FMA-only sqrt and division
@@ -121,13 +157,16 @@ __device__ __forceinline__ float warp_absmax(float acc) {
     return acc;
 }
 
-// scales.clamp(min=1e-12) (spatial_8bit.py:96), NaN passes through
-__device__ __forceinline__ float block_scale(float absmax) { return absmax < 1e-12f ? 1e-12f : absmax; }
+// scales.clamp(min=1e-12) (spatial_8bit.py:96), NaN passes through; in the
+// moments' dtype (fp16 has no 1e-12: an all-zero block gets scale 0)
+template <class T = float>
+__device__ __forceinline__ float block_scale(float absmax) { return rd<T>(absmax < 1e-12f ? 1e-12f : absmax); }
 
 // q = round(x / s * 127) half-to-even, dead-zone lift, clamp +-127
 // (spatial_8bit.py:97-106).  NaN is stored as 0.
+template <class T = float>
 __device__ __forceinline__ int8_t quantize1(float x, float s) {
-    float r = rintf(__fmul_rn(__fdiv_rn(x, s), 127.0f));
+    float r = rintf(rd<T>(__fmul_rn(rd<T>(__fdiv_rn(x, s)), 127.0f)));
     if (r == 0.0f && x != 0.0f && x == x) r = x > 0.0f ? 1.0f : -1.0f;
     r = r > 127.0f ? 127.0f : r;
     r = r < -127.0f ? -127.0f : r;
@@ -135,8 +174,10 @@ __device__ __forceinline__ int8_t quantize1(float x, float s) {
 }
 
 // q * (s / 127)  (spatial_8bit.py:118)
-__device__ __forceinline__ float dequant_step(float s) { return __fdiv_rn(s, 127.0f); }
-__device__ __forceinline__ float dequant1(int8_t q, float t) { return __fmul_rn((float)q, t); }
+template <class T = float>
+__device__ __forceinline__ float dequant_step(float s) { return rd<T>(__fdiv_rn(s, 127.0f)); }
+template <class T = float>
+__device__ __forceinline__ float dequant1(int8_t q, float t) { return rd<T>(__fmul_rn((float)q, t)); }
 
 // ---------------------------------------------------------------- bilinear
 
@@ -192,26 +233,30 @@ __device__ __forceinline__ Coef row_coef(int64_t r, int64_t H, int64_t h, int64_
 }
 
 // torch's separable bilinear (output H+W > 128): width pass, then height pass
-__device__ __forceinline__ float interp_generic(const float *src, int64_t w, const Coef &rc, const Coef &cc,
+// (src elements of type S; the result in fp32, before any rounding to a dtype)
+template <class S = float>
+__device__ __forceinline__ float interp_generic(const S *src, int64_t w, const Coef &rc, const Coef &cc,
                                                 int64_t r, int64_t q) {
-    if (rc.ident && cc.ident) return src[r * w + q];
+    if (rc.ident && cc.ident) return ld<S>(src + r * w + q);
     if (rc.ident) {
-        const float *s = src + r * w;
-        return __fmaf_rn(s[cc.i0], cc.l0, __fmul_rn(s[cc.i1], cc.l1));
+        const S *s = src + r * w;
+        return __fmaf_rn(ld<S>(s + cc.i0), cc.l0, __fmul_rn(ld<S>(s + cc.i1), cc.l1));
     }
-    if (cc.ident) return __fmaf_rn(src[rc.i0 * w + q], rc.l0, __fmul_rn(src[rc.i1 * w + q], rc.l1));
-    const float *s0 = src + rc.i0 * w, *s1 = src + rc.i1 * w;
-    float t0 = __fmaf_rn(s0[cc.i0], cc.l0, __fmul_rn(s0[cc.i1], cc.l1));
-    float t1 = __fmaf_rn(s1[cc.i0], cc.l0, __fmul_rn(s1[cc.i1], cc.l1));
+    if (cc.ident)
+        return __fmaf_rn(ld<S>(src + rc.i0 * w + q), rc.l0, __fmul_rn(ld<S>(src + rc.i1 * w + q), rc.l1));
+    const S *s0 = src + rc.i0 * w, *s1 = src + rc.i1 * w;
+    float t0 = __fmaf_rn(ld<S>(s0 + cc.i0), cc.l0, __fmul_rn(ld<S>(s0 + cc.i1), cc.l1));
+    float t1 = __fmaf_rn(ld<S>(s1 + cc.i0), cc.l0, __fmul_rn(ld<S>(s1 + cc.i1), cc.l1));
     return __fmaf_rn(t0, rc.l0, __fmul_rn(t1, rc.l1));
 }
 
 // torch's channels-last bilinear kernel (used when output H+W <= 128)
-__device__ __forceinline__ float interp_small(const float *src, int64_t w, const Coef &rc, const Coef &cc) {
+template <class S = float>
+__device__ __forceinline__ float interp_small(const S *src, int64_t w, const Coef &rc, const Coef &cc) {
     float w00 = __fmul_rn(rc.l0, cc.l0), w01 = __fmul_rn(rc.l0, cc.l1);
     float w10 = __fmul_rn(rc.l1, cc.l0), w11 = __fmul_rn(rc.l1, cc.l1);
-    float a = src[rc.i0 * w + cc.i0], b = src[rc.i0 * w + cc.i1];
-    float c = src[rc.i1 * w + cc.i0], d = src[rc.i1 * w + cc.i1];
+    float a = ld<S>(src + rc.i0 * w + cc.i0), b = ld<S>(src + rc.i0 * w + cc.i1);
+    float c = ld<S>(src + rc.i1 * w + cc.i0), d = ld<S>(src + rc.i1 * w + cc.i1);
     return __fmaf_rn(d, w11, __fmaf_rn(c, w10, __fmaf_rn(a, w00, __fmul_rn(b, w01))));
 }
 
@@ -222,7 +267,8 @@ __device__ __forceinline__ float interp_small(const float *src, int64_t w, const
 // With rp / cp set the window is taken in the permuted basis: its row r and
 // column c are view row rp[r] and column cp[c] (g[rp][:, cp] of
 // spatial_8bit.py:235-237).
-__device__ __forceinline__ void pool_cell(const float *__restrict__ g, const float *__restrict__ p, int64_t H,
+template <class T = float>
+__device__ __forceinline__ void pool_cell(const T *__restrict__ g, const T *__restrict__ p, int64_t H,
                                           int64_t W, int64_t h, int64_t w, int exact, int64_t i, int64_t j,
                                           const smo_hyper &hp, float &mean, float &sq_mean,
                                           const int64_t *rp = nullptr, const int64_t *cp = nullptr) {
@@ -238,22 +284,22 @@ __device__ __forceinline__ void pool_cell(const float *__restrict__ g, const flo
     float s1 = 0.0f, s2 = 0.0f;
     for (int64_t r = r0; r < r1; r++) {
         const int64_t vr = rp ? rp[r] : r;
-        const float *gr = g + vr * W, *pr = p + vr * W;
+        const T *gr = g + vr * W, *pr = p + vr * W;
         for (int64_t c = c0; c < c1; c++) {
             const int64_t vc = cp ? cp[c] : c;
-            float x = decayed(gr[vc], pr[vc], hp);
+            float x = decayed<T>(ld<T>(gr + vc), ld<T>(pr + vc), hp);
             s1 = __fadd_rn(s1, x);
-            s2 = __fadd_rn(s2, __fmul_rn(x, x));
+            s2 = __fadd_rn(s2, rd<T>(__fmul_rn(x, x)));  // torch.square, then the pool
         }
     }
     if (exact) {
         float div = (float)((r1 - r0) * (c1 - c0));
-        mean = __fdiv_rn(s1, div);
-        sq_mean = __fdiv_rn(s2, div);
+        mean = rd<T>(__fdiv_rn(s1, div));
+        sq_mean = rd<T>(__fdiv_rn(s2, div));
     } else {
         float dh = (float)(r1 - r0), dw = (float)(c1 - c0);
-        mean = __fdiv_rn(__fdiv_rn(s1, dh), dw);
-        sq_mean = __fdiv_rn(__fdiv_rn(s2, dh), dw);
+        mean = rd<T>(__fdiv_rn(__fdiv_rn(s1, dh), dw));
+        sq_mean = rd<T>(__fdiv_rn(__fdiv_rn(s2, dh), dw));
     }
 }
 

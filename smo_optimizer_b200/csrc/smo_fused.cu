@@ -811,6 +811,7 @@ static int64_t strip_rows(const smo_tensor &t, int64_t target) {
 bool fused_takes(const smo_tensor &t) {
     if (t.kind != SMO_KIND_POOLED8 && t.kind != SMO_KIND_POOLED32) return false;
     if (t.flags & SMO_FLAG_GENERAL_PATH) return false;
+    if (t.dtype != SMO_DTYPE_F32) return false;  // half-precision tensors take the general kernels
     if (t.row_perm || t.col_perm || t.row_perm_inv || t.col_perm_inv) return false;  // permute_basis
     if (t.rows <= 0 || t.cols <= 0 || t.comp_rows <= 0 || t.comp_cols <= 0) return false;
     if (t.rows % t.comp_rows != 0 || t.cols % t.comp_cols != 0) return false;

@@ -16,7 +16,9 @@ constexpr int64_t kDenseChunk = 1024;   // elements per DENSE work item
 constexpr int64_t kPooled32Chunk = 64;  // compact cells per POOLED32 work item
 constexpr size_t kScratchAlign = 256;
 
-// Validated per-tensor descriptor as the kernels see it.
+// Validated per-tensor descriptor as the kernels see it.  The float pointers
+// of p, g, scales and POOLED32 / DENSE moments point at elements of type dtype
+// (the kernels cast them); codes are int8 and POOLED8 scratch is fp32.
 struct DevDesc {
     float *p;
     const float *g;
@@ -36,7 +38,7 @@ struct DevDesc {
     int32_t kind;
     int32_t exact;  // whole windows tile the view
     int32_t same;   // identity interpolation (h == H, w == W, monolithic)
-    int32_t pad_;
+    int32_t dtype;  // smo_dtype of p, g, scales and POOLED32 / DENSE moments
     smo_hyper hp;
     // permute_basis: pooling basis (rp, cp) and its inverse (rpi, cpi); null = identity
     const int64_t *rp, *cp, *rpi, *cpi;

@@ -7,7 +7,11 @@ the per-tensor arithmetic runs in the CUDA library (include/smo_b200.h), one
 ``smo_step`` call per device per step, on the current CUDA stream.
 
 Differences a user can observe:
-  * Tensors must live on a CUDA device and be fp32; there is no CPU path.
+  * Tensors must live on a CUDA device; there is no CPU path.  Parameters
+    are fp32, bf16 or fp16 with gradients of the same dtype; as in the
+    reference, the state's block scales and float moments take the
+    parameter's dtype and every op rounds to it.  Half-precision tensors are
+    stepped by the general two-launch kernels (the fused kernel is fp32-only).
   * Pooled moments are double-buffered: after a step ``state[p]['m_q']`` (and
     the other moment tensors) refer to the buffer the step wrote, and the
     previous buffer is reused two steps later.  ``state_dict()`` returns live
@@ -74,19 +78,31 @@ def _same_dense_layout(*tensors) -> bool:
     return True
 
 
+# torch dtype -> smo_dtype code of the descriptor
+_DTYPE_CODES = {torch.float32: _lib.SMO_DTYPE_F32, torch.bfloat16: _lib.SMO_DTYPE_BF16,
+                torch.float16: _lib.SMO_DTYPE_F16}
+
+
+def _check_state(p, state, expected):
+    """Raise TypeError unless each present state tensor has its expected dtype
+    and lives on the parameter's device; codes, scales and permutations must
+    also be contiguous (full-resolution moments follow the parameter's layout,
+    which the step checks itself)."""
+    for key, dtype in expected:
+        t = state.get(key)
+        if not torch.is_tensor(t):
+            continue
+        contiguous = t.is_contiguous() or key in ("exp_avg", "exp_avg_sq")
+        if t.dtype != dtype or t.device != p.device or not contiguous:
+            raise TypeError(f"state['{key}'] must be a contiguous {dtype} tensor on {p.device}; "
+                            f"got {t.dtype} on {t.device}")
+
+
 def _named(params):
     params = list(params)
     if params and isinstance(params[0], tuple) and len(params[0]) == 2 and isinstance(params[0][0], str):
         return params
     raise ValueError("protect_output needs named parameters: pass model.named_parameters()")
-
-
-class _Plan:
-    """Cached descriptor table of one device's tensors (rebuilt when the set changes)."""
-
-    def __init__(self, key, table):
-        self.key = key
-        self.table = table
 
 
 class _SpatialBase(Optimizer):
@@ -109,9 +125,10 @@ class _SpatialBase(Optimizer):
 
     # ---------------------------------------------------------------- state
 
-    # dtypes of the state tensors that are not the parameter's dtype
-    _STATE_DTYPES = (("m_q", torch.int8), ("v_q", torch.int8), ("m_s", torch.float32), ("v_s", torch.float32),
-                     ("row_perm", torch.int64), ("col_perm", torch.int64))
+    # dtypes of the state tensors that are not the parameter's dtype (block
+    # scales and fp32-kind moments have the parameter's dtype)
+    _STATE_DTYPES = (("m_q", torch.int8), ("v_q", torch.int8), ("row_perm", torch.int64), ("col_perm", torch.int64))
+    _PARAM_DTYPE_STATE = ("m_s", "v_s", "exp_avg", "exp_avg_sq")
 
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)
@@ -173,9 +190,9 @@ class _SpatialBase(Optimizer):
                 if p.device.type != "cuda":
                     raise RuntimeError(f"{self._name} (B200 build) steps CUDA tensors only; "
                                        f"got a parameter on {p.device}")
-                if p.dtype != torch.float32 or grad.dtype != torch.float32:
-                    raise TypeError(f"{self._name} (B200 build) supports fp32 parameters and gradients; "
-                                    f"got {p.dtype} / {grad.dtype}")
+                if p.dtype not in _DTYPE_CODES or grad.dtype != p.dtype:
+                    raise TypeError(f"{self._name} (B200 build) steps fp32, bf16 or fp16 parameters with "
+                                    f"gradients of the same dtype; got {p.dtype} / {grad.dtype}")
                 state = self.state[p]
                 if "step" not in state:
                     self._init_state(p, grad, group)
@@ -383,9 +400,9 @@ class SMO8bit(_SpatialBase):
             state["q_block"] = qb
             nb = _host.num_blocks(grad.numel(), qb)
             state["m_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
-            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=grad.dtype, device=dev)
             state["v_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
-            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=grad.dtype, device=dev)
             return
         view = _host.compression_view(grad.shape, self.compress_conv) if raw else None
         if view is not None and p.is_contiguous():
@@ -398,11 +415,12 @@ class SMO8bit(_SpatialBase):
             qb = _host.pooled_q_block(pshape, cs, group["block_size"])
             state["q_block"] = qb
             nb = _host.num_blocks(cs[0] * cs[1], qb)
-            # quantising zeros gives zero codes and 1e-12 scales (spatial_8bit.py:195-200)
+            # quantising zeros gives zero codes and 1e-12 scales in the gradient's
+            # dtype (spatial_8bit.py:195-200; 0 in fp16, which has no 1e-12)
             state["m_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
-            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["m_s"] = torch.full((nb, 1), 1e-12, dtype=grad.dtype, device=dev)
             state["v_q"] = torch.zeros((nb, qb), dtype=torch.int8, device=dev)
-            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=torch.float32, device=dev)
+            state["v_s"] = torch.full((nb, 1), 1e-12, dtype=grad.dtype, device=dev)
             state["comp_shape"] = cs
             if self.permute_basis:
                 # random basis permutations drawn as the reference does
@@ -441,11 +459,8 @@ class SMO8bit(_SpatialBase):
         return sp
 
     def _fill(self, rec, p, grad, state, group):
-        for key, dtype in self._STATE_DTYPES:
-            t = state.get(key)
-            if t is not None and (t.dtype != dtype or t.device != p.device or not t.is_contiguous()):
-                raise TypeError(f"state['{key}'] must be a contiguous {dtype} tensor on {p.device}; "
-                                f"got {t.dtype} on {t.device}")
+        _check_state(p, state, self._STATE_DTYPES + tuple((k, p.dtype) for k in self._PARAM_DTYPE_STATE))
+        rec["dtype"] = _DTYPE_CODES[p.dtype]
         rec["param"] = p.data_ptr()
         rec["grad"] = grad.data_ptr()
         rec["flags"] = self._kernel_flags
@@ -543,6 +558,8 @@ class SMO(_SpatialBase):
             state["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
 
     def _fill(self, rec, p, grad, state, group):
+        _check_state(p, state, tuple((k, p.dtype) for k in ("exp_avg", "exp_avg_sq")))
+        rec["dtype"] = _DTYPE_CODES[p.dtype]
         rec["param"] = p.data_ptr()
         rec["grad"] = grad.data_ptr()
         rec["flags"] = self._kernel_flags
@@ -550,6 +567,8 @@ class SMO(_SpatialBase):
         if state["is_compressed"]:
             if not p.is_contiguous():
                 raise RuntimeError("a pooled parameter must stay contiguous (it was at init)")
+            if not (state["exp_avg"].is_contiguous() and state["exp_avg_sq"].is_contiguous()):
+                raise TypeError("pooled moments state['exp_avg'] / state['exp_avg_sq'] must be contiguous")
             rec["kind"] = _lib.SMO_KIND_POOLED32
             rec["rows"], rec["cols"] = state["orig_shape"]
             rec["comp_rows"], rec["comp_cols"] = state["exp_avg"].shape

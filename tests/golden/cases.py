@@ -14,7 +14,8 @@ from smo_optimizer_b200 import synthetic
 
 HP = dict(lr=1e-3, betas=(0.9, 0.999), eps=1e-8)
 
-# name -> dict(opt, kwargs, tensors=[(shape, group_index)], groups=[{...}], steps, seed, bf16)
+# name -> dict(opt, kwargs, tensors=[(shape, group_index)], groups=[{...}], steps, seed, bf16,
+#              param_dtype ("bfloat16" / "float16": params, grads and state in that dtype), grad_std)
 CASES = {
     # the single-weight parity workload: 1024x1024, k=0.25, 100 steps
     "single1024": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64),
@@ -80,6 +81,27 @@ CASES = {
                           tensors=[((512, 1536), 0), ((2048, 512), 0), ((512,), 0), ((256, 256), 1)],
                           groups=[{"compress": True}, {"compress": False}], steps=3, seed=22, bf16=True,
                           sample_stride=17),
+    # half-precision parameters: the reference computes in the parameter's
+    # dtype, its moments and block scales included
+    "bf16_s8_mono": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64),
+                         tensors=[((128, 256), 0), ((300,), 0), ((64, 40), 0)], steps=3, seed=23,
+                         param_dtype="bfloat16"),
+    "bf16_s8_band_groups": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64,
+                                                           low_peak=True, band_mb=0.03),
+                                tensors=[((256, 512), 0), ((50, 30), 0), ((64, 64), 1), ((48, 32), 2), ((100,), 2)],
+                                groups=[{"compress": True}, {"compress": False}, {"compress": "quant_only"}],
+                                steps=3, seed=24, param_dtype="bfloat16"),
+    "bf16_smo": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
+                     tensors=[((96, 192), 0), ((192,), 0), ((100, 200), 0)], steps=3, seed=25, param_dtype="bfloat16"),
+    "fp16_s8_groups": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.25, block_size=64),
+                           tensors=[((128, 256), 0), ((300,), 0), ((64, 64), 1), ((48, 32), 2)],
+                           groups=[{"compress": True}, {"compress": False}, {"compress": "quant_only"}],
+                           steps=3, seed=26, param_dtype="float16", grad_std=0.05),
+    "fp16_s8_band": dict(opt="SMO8bit", kwargs=dict(HP, weight_decay=0.0, k_ratio=0.25, block_size=64,
+                                                    low_peak=True, band_mb=0.03),
+                         tensors=[((256, 512), 0)], steps=3, seed=27, param_dtype="float16", grad_std=0.05),
+    "fp16_smo": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
+                     tensors=[((96, 192), 0), ((192,), 0)], steps=3, seed=28, param_dtype="float16", grad_std=0.05),
     # SMO-Spatial fp32 pooled moments
     "smo_96x192_k05": dict(opt="SMO", kwargs=dict(HP, weight_decay=0.01, k_ratio=0.5),
                            tensors=[((96, 192), 0), ((192,), 0)], steps=5, seed=13),
@@ -99,14 +121,30 @@ STATE_META_KEYS = ("step", "is_compressed", "is_quant_only", "orig_shape", "para
                    "q_block", "comp_shape", "q_shape", "q_numel")
 
 
+def round_to_dtype(x, dtype):
+    """fp32 values rounded to ``dtype`` ("float32", "bfloat16", "float16"), as fp32."""
+    if dtype == "bfloat16":
+        return synthetic.round_to_bf16(x)
+    if dtype == "float16":
+        return np.ascontiguousarray(x, np.float32).astype(np.float16).astype(np.float32)
+    return x
+
+
+def case_dtype(case):
+    return case.get("param_dtype", "float32")
+
+
 def case_params(case):
-    """Initial parameter arrays (fp32 ~N(0, 0.02))."""
-    return [synthetic.synth_param(case["seed"], i, shape) for i, (shape, _) in enumerate(case["tensors"])]
+    """Initial parameter arrays (~N(0, 0.02), values of the case's parameter dtype, as fp32)."""
+    return [round_to_dtype(synthetic.synth_param(case["seed"], i, shape), case_dtype(case))
+            for i, (shape, _) in enumerate(case["tensors"])]
 
 
 def case_grads(case, step):
-    """Gradients for 1-based ``step`` (fp32 ~N(0, 1e-3))."""
-    return [synthetic.synth_grad(case["seed"], step, i, shape, bf16=case.get("bf16", False))
+    """Gradients for 1-based ``step`` (~N(0, grad_std = 1e-3), values of the parameter dtype)."""
+    std = case.get("grad_std", 1e-3)
+    return [round_to_dtype(synthetic.synth_grad(case["seed"], step, i, shape, std=std, bf16=case.get("bf16", False)),
+                           case_dtype(case))
             for i, (shape, _) in enumerate(case["tensors"])]
 
 

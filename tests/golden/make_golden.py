@@ -54,20 +54,21 @@ def main():
     names = args.cases or list(C.CASES)
     for name in names:
         case = C.CASES[name]
-        params = [torch.nn.Parameter(torch.from_numpy(a.copy())) for a in C.case_params(case)]
+        tdtype = getattr(torch, C.case_dtype(case))
+        params = [torch.nn.Parameter(torch.from_numpy(a.copy()).to(tdtype)) for a in C.case_params(case)]
         groups = C.case_groups(case, params)
         cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
         opt = cls(groups, **case["kwargs"])
         torch.manual_seed(case["seed"])  # permute_basis draws its permutations at the first step
         for step in range(1, case["steps"] + 1):
             for p, g in zip(params, C.case_grads(case, step)):
-                p.grad = torch.from_numpy(g.copy())
+                p.grad = torch.from_numpy(g.copy()).to(tdtype)
             opt.step()
         out = {}
-        meta = {"case": name, "torch": torch.__version__, "tensors": []}
+        meta = {"case": name, "torch": torch.__version__, "param_dtype": C.case_dtype(case), "tensors": []}
         stride = case.get("sample_stride")
         for i, p in enumerate(params):
-            arr = p.detach().numpy().reshape(-1)
+            arr = p.detach().float().numpy().reshape(-1)  # half-precision values are exact in fp32
             if stride:
                 out[f"{i}.param_sample"] = arr[C.sample_indices(arr.size, stride)].copy()
             else:
@@ -81,7 +82,8 @@ def main():
             meta["tensors"].append(tmeta)
             for k in C.STATE_ARRAY_KEYS:
                 if k in st:
-                    out[f"{i}.{k}"] = st[k].detach().numpy().copy()
+                    t = st[k].detach()
+                    out[f"{i}.{k}"] = (t.float() if t.is_floating_point() else t).numpy().copy()
         if name in STATE_DICT_CASES:
             sd_path = os.path.join(HERE, f"{name}.state.pt")
             torch.save(opt.state_dict(), sd_path)

@@ -7,7 +7,9 @@ Expected agreement:
   * with the oracle: bit-identical codes, scales, moments and params (both
     sides round every fp32 operation the same way, IEEE sqrt included);
   * with the reference (golden files): codes bit-identical except <= 1e-5 of
-    them by one LSB, scales and params within rtol 1e-5 / atol 1e-7.
+    them by one LSB, scales and params within rtol 1e-5 / atol 1e-7;
+    half-precision cases within _golden.half_close (the elements torch's
+    scalar tail loop rounds differently).
 """
 
 import numpy as np
@@ -15,7 +17,7 @@ import pytest
 import torch
 
 import cases as C
-from _golden import code_mismatch_fraction, golden_perms, load
+from _golden import code_mismatch_fraction, golden_perms, half_close, load
 from oracle import oracle
 from smo_optimizer_b200 import SMO, SMO8bit, _host, _lib, ops, synthetic
 
@@ -32,12 +34,20 @@ def _cuda():
     _lib.load()
 
 
-def cuda(a):
-    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+TORCH_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def cuda(a, dtype="float32"):
+    """Host array to the GPU; floating arrays in ``dtype`` (their values are of that dtype already)."""
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(TORCH_DTYPES[dtype]) if t.is_floating_point() else t
 
 
 def host(t):
-    return t.detach().cpu().numpy()
+    t = t.detach()
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.float()  # exact: every half value is an fp32 value
+    return t.cpu().numpy()
 
 
 # ------------------------------------------------------------------ stages
@@ -119,7 +129,8 @@ def test_fastmath_selftest_matches_ieee():
 
 def run_gpu_case(name, steps=None, general=False):
     case = C.CASES[name]
-    params = [torch.nn.Parameter(cuda(a)) for a in C.case_params(case)]
+    dt = C.case_dtype(case)
+    params = [torch.nn.Parameter(cuda(a, dt)) for a in C.case_params(case)]
     groups = C.case_groups(case, params)
     cls = SMO8bit if case["opt"] == "SMO8bit" else SMO
     opt = cls(groups, **case["kwargs"])
@@ -131,7 +142,7 @@ def run_gpu_case(name, steps=None, general=False):
         opt._kernel_flags = 1  # SMO_FLAG_GENERAL_PATH
     for step in range(1, (steps or case["steps"]) + 1):
         for p, g in zip(params, C.case_grads(case, step)):
-            p.grad = cuda(g)
+            p.grad = cuda(g, dt)
         opt.step()
     torch.cuda.synchronize()
     assert opt.workspace_status() == 0, "device-side status reports a failure"
@@ -142,7 +153,7 @@ def run_oracle_case(name, steps=None):
     case = C.CASES[name]
     params = C.case_params(case)
     groups = C.case_groups(case, params)
-    opt = oracle.OracleOptimizer(case["opt"], groups, **case["kwargs"])
+    opt = oracle.OracleOptimizer(case["opt"], groups, param_dtype=C.case_dtype(case), **case["kwargs"])
     keys = [k for k, _, _ in opt.params()]
     for k, pr in zip(keys, golden_perms(name, len(keys))):
         if pr is not None:
@@ -157,21 +168,31 @@ ALL_CASES = [n for n in C.CASES if n != "single1024"]
 
 @pytest.mark.parametrize("name", ALL_CASES)
 def test_step_bit_exact_vs_oracle(name):
+    """Every case, fp32 and half precision: bit-identical to the oracle (for
+    half-precision cases the fp16 eps underflow makes some parameters NaN or
+    infinite, in the reference too; those match as values)."""
     gp, gs = run_gpu_case(name)
     op, os_ = run_oracle_case(name)
+    dt = C.case_dtype(C.CASES[name])
     for i, (p, st, ref_p, ref_st) in enumerate(zip(gp, gs, op, os_)):
+        assert p.dtype == TORCH_DTYPES[dt]
         for k in C.STATE_ARRAY_KEYS:
             if k in ref_st:
                 got = host(st[k]).reshape(-1)
                 ref = np.asarray(ref_st[k]).reshape(-1)
-                assert np.array_equal(got, ref), f"{name}[{i}] {k} differs from the oracle"
-        assert np.array_equal(host(p).reshape(-1), ref_p.reshape(-1)), f"{name}[{i}] param differs from the oracle"
+                if k in ("m_s", "v_s", "exp_avg", "exp_avg_sq"):
+                    assert st[k].dtype == TORCH_DTYPES[dt], f"{name}[{i}] {k} dtype"
+                assert np.array_equal(got, ref, equal_nan=got.dtype != np.int8), \
+                    f"{name}[{i}] {k} differs from the oracle"
+        assert np.array_equal(host(p).reshape(-1), ref_p.reshape(-1), equal_nan=True), \
+            f"{name}[{i}] param differs from the oracle"
 
 
 @pytest.mark.parametrize("name", ALL_CASES + ["single1024"])
 def test_step_matches_reference_goldens(name):
     gp, gs = run_gpu_case(name)
     case = C.CASES[name]
+    dt = C.case_dtype(case)
     gold, meta = load(name)
     stride = case.get("sample_stride")
     for i, (p, st) in enumerate(zip(gp, gs)):
@@ -186,12 +207,17 @@ def test_step_matches_reference_goldens(name):
                 continue
             ref = gold[gk]
             got = host(st[k]).reshape(ref.shape)
-            if ref.dtype == np.int8:
+            if dt != "float32":
+                half_close(got, ref, dt, f"{name}[{i}] {k}")
+            elif ref.dtype == np.int8:
                 assert code_mismatch_fraction(got, ref) <= CODE_FRAC
             else:
                 np.testing.assert_allclose(got, ref, rtol=RTOL, atol=ATOL)
         flat = host(p).reshape(-1)
-        if stride:
+        if dt != "float32":
+            half_close(flat[C.sample_indices(flat.size, stride)] if stride else flat,
+                       gold[f"{i}.param_sample"] if stride else gold[f"{i}.param"], dt, f"{name}[{i}] param")
+        elif stride:
             np.testing.assert_allclose(flat[C.sample_indices(flat.size, stride)], gold[f"{i}.param_sample"],
                                        rtol=RTOL, atol=ATOL)
         else:

@@ -36,7 +36,7 @@ def test_library_exports_every_declared_symbol():
 def test_binding_layout_matches_library():
     lib = _lib.load()
     assert lib.smo_abi_version() == _lib.ABI_VERSION
-    assert lib.smo_tensor_struct_size() == _lib.TENSOR_DTYPE.itemsize == 240
+    assert lib.smo_tensor_struct_size() == _lib.TENSOR_DTYPE.itemsize == 248
 
 
 def test_status_strings_and_host_side_validation():
@@ -57,6 +57,30 @@ def test_status_strings_and_host_side_validation():
     t["param"] = 256
     assert lib.smo_step(t.ctypes.data, 1, None, 0, None) == 1              # dense: no pointers for m/v
     assert lib.smo_step(t.ctypes.data, 0, addr, 2048, None) == 0           # empty step is a no-op
+
+
+def test_dtype_field_rules():
+    """smo_tensor.dtype: 0 fp32, 1 bf16, 2 fp16, anything else is invalid;
+    half-precision pointers need 2-byte alignment, fp32 ones 4."""
+    lib = _lib.load()
+    ws = (ctypes.c_uint8 * 4096)()
+    addr = (ctypes.addressof(ws) + 255) // 256 * 256
+    t = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+    t["kind"], t["rows"], t["cols"] = _lib.SMO_KIND_DENSE, 16, 1
+    t["param"] = 258                                                          # 2-byte aligned only
+    t["grad"] = 512
+    t["dtype"] = 3
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 1           # unknown dtype
+    t["dtype"] = _lib.SMO_DTYPE_F32
+    assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 2           # fp32 needs 4 bytes
+    for dt in (_lib.SMO_DTYPE_BF16, _lib.SMO_DTYPE_F16):
+        t["dtype"] = dt
+        # alignment accepted; the missing moment pointers are what is reported
+        assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 1
+        t["m_in"], t["v_in"], t["m_out"] = 1024, 2048, 4096
+        t["v_out"] = 8193                                                     # odd: misaligned half
+        assert lib.smo_step(t.ctypes.data, 1, addr, 2048, None) == 2
+        t["m_in"] = t["v_in"] = t["m_out"] = t["v_out"] = 0
 
 
 def test_no_alloc_validates_before_touching_its_scratch():

@@ -4,13 +4,20 @@ must reproduce the reference's own outputs (written by make_golden.py).
 Tolerances are the parity contract of the step:
   * int8 codes bit-identical, except at most 1e-5 of them off by one LSB;
   * scales and params within rtol 1e-5 / atol 1e-7 (fp32).
+
+Half-precision parameters (bf16 / fp16 cases): the oracle computes every op
+as torch's vectorised CPU loop does (fp32 arithmetic, one rounding to the
+dtype per op); the elements torch's scalar tail loop rounds differently are
+covered by _golden.half_close (at most 2 % of an array's elements differ,
+codes by one LSB, values by at most 2^-6 (bf16) / 2^-8 (fp16) of the
+array's largest finite magnitude; NaN and infinities match).
 """
 
 import numpy as np
 import pytest
 
 import cases as C
-from _golden import code_mismatch_fraction, golden_perms, load
+from _golden import code_mismatch_fraction, golden_perms, half_close, load
 from oracle import oracle
 
 CODE_FRAC = 1e-5
@@ -23,7 +30,7 @@ def run_oracle(name):
     groups = C.case_groups(case, params)
     assert [gi for _, gi in case["tensors"]] == sorted(gi for _, gi in case["tensors"])
     kw = dict(case["kwargs"])
-    opt = oracle.OracleOptimizer(case["opt"], groups, **kw)
+    opt = oracle.OracleOptimizer(case["opt"], groups, param_dtype=C.case_dtype(case), **kw)
     keys = [k for k, _, _ in opt.params()]
     for k, pr in zip(keys, golden_perms(name, len(keys))):
         if pr is not None:
@@ -35,6 +42,7 @@ def run_oracle(name):
 
 def compare_to_golden(name, params, states, code_frac=CODE_FRAC, rtol=RTOL, atol=ATOL):
     case = C.CASES[name]
+    dtype = C.case_dtype(case)
     gold, meta = load(name)
     stride = case.get("sample_stride")
     for i, (p, st) in enumerate(zip(params, states)):
@@ -50,13 +58,18 @@ def compare_to_golden(name, params, states, code_frac=CODE_FRAC, rtol=RTOL, atol
                 continue
             ref = gold[gk]
             got = np.asarray(st[k]).reshape(ref.shape)
-            if ref.dtype == np.int8:
+            if dtype != "float32":
+                half_close(got, ref, dtype, f"{name}[{i}] {k}")
+            elif ref.dtype == np.int8:
                 frac = code_mismatch_fraction(got, ref)
                 assert frac <= code_frac, f"{name}[{i}] {k}: {frac:.2e} of codes differ"
             else:
                 np.testing.assert_allclose(got, ref, rtol=rtol, atol=atol, err_msg=f"{name}[{i}] {k}")
         flat = np.asarray(p).reshape(-1)
-        if stride:
+        if dtype != "float32":
+            half_close(flat[C.sample_indices(flat.size, stride)] if stride else flat,
+                       gold[f"{i}.param_sample"] if stride else gold[f"{i}.param"], dtype, f"{name}[{i}] param")
+        elif stride:
             np.testing.assert_allclose(flat[C.sample_indices(flat.size, stride)], gold[f"{i}.param_sample"],
                                        rtol=rtol, atol=atol, err_msg=f"{name}[{i}] param")
         else:
