@@ -481,10 +481,16 @@ def main():
     time.sleep(0.3)
     launches0 = lib.smo_launch_count()
     t_start.record(stream)
+    host_t = []
     for k in range(K):
         ev[k][0].record(stream)
+        h0 = time.perf_counter()
         opt.step()
+        host_t.append(time.perf_counter() - h0)
         ev[k][1].record(stream)
+    # host time of one step() call: the median of the first ten (launches are
+    # asynchronous; later calls of a long run can wait for room in the launch queue)
+    host_ms = float(np.median(host_t[:10])) * 1e3
     t_end.record(stream)
     torch.cuda.synchronize()
     launches = lib.smo_launch_count() - launches0
@@ -664,6 +670,7 @@ def main():
                                                    "params": my_params} if shard_of else {})),
             "hbm_gbs": (my_bytes if shard_of else sum(costs)) / (ms_per_step * 1e-3) / 1e9,
             "kernel_ms_per_step": step_ms,
+            "host_ms_per_step": host_ms,
             "roofline": roof,
             "cpu_baseline": cpu_ref or cpu,
             "cpu_baseline_port": cpu,

@@ -25,6 +25,7 @@ Differences a user can observe:
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import numpy as np
@@ -98,6 +99,97 @@ def _check_state(p, state, expected):
                             f"got {t.dtype} on {t.device}")
 
 
+# descriptor fields a step reads (in) and writes (out) for the double-buffered kinds
+_IN_OUT = {
+    _lib.SMO_KIND_POOLED8: (("m_q_in", "m_q_out"), ("m_s_in", "m_s_out"), ("v_q_in", "v_q_out"),
+                            ("v_s_in", "v_s_out")),
+    _lib.SMO_KIND_POOLED32: (("m_in", "m_out"), ("v_in", "v_out")),
+}
+
+
+class _StepPlan:
+    """The C++ host path of one optimizer's parameter set (csrc/smo_host.cpp).
+
+    Built after a step of the Python path, when every parameter with a
+    gradient lives on one CUDA device, needs no staged copies and has no
+    basis permutation: one entry per parameter of every group with the
+    descriptor for each moment-buffer parity.  ``run`` does the whole step in
+    one C++ call and returns 0, -1 when the plan no longer applies (nothing
+    was modified; the caller steps through the Python path) or an smo_status.
+    """
+
+    __slots__ = ("ext", "cap", "flags", "state", "ws")
+
+    @staticmethod
+    def build(opt):
+        if type(opt)._launch is not _SpatialBase._launch:
+            return None  # a subclass that launches its own way keeps the Python path
+        entries, dev = [], None
+        for gi, group in enumerate(opt.param_groups):
+            for p in group["params"]:
+                grad = p.grad
+                if grad is None:
+                    entries.append((p, None))
+                    continue
+                state = opt.state.get(p)
+                if not state or "step" not in state or "row_perm" in state or p.device.type != "cuda":
+                    return None
+                if dev is None:
+                    dev = p.device
+                elif p.device != dev:
+                    return None
+                kp, kg, kst, back = opt._stage(p, grad, state)
+                if back is not None or kp is not p or kg is not grad or kst is not state:
+                    return None
+                rec = np.zeros(1, dtype=_lib.TENSOR_DTYPE)
+                opt._fill(rec[0], p, grad, state, group)
+                keys, double = opt._moment_keys(state)
+                cur = tuple(state[k] for k in keys)
+                other = opt._other(p, state, keys) if double else cur
+                row0 = rec.tobytes()
+                if double:
+                    for a, b in _IN_OUT[int(rec["kind"][0])]:
+                        rec[a], rec[b] = rec[b].copy(), rec[a].copy()
+                dense = not state.get("is_compressed") and not state.get("is_quant_only")
+                entries.append((p, state, gi, double, keys, cur, other, row0, rec.tobytes(), dense))
+        ws = opt._workspace.get(dev.index) if dev is not None else None
+        if ws is None:
+            return None
+        ext = _host_ext()
+        fn = ctypes.cast(_lib.load().smo_step, ctypes.c_void_p).value
+        try:
+            cap = ext.plan_new(opt.param_groups, opt.state, entries, dev.index, ws.data_ptr(), ws.numel(), fn)
+        except (RuntimeError, ValueError):
+            return None
+        plan = _StepPlan()
+        plan.ext, plan.cap, plan.flags, plan.state, plan.ws = ext, cap, opt._kernel_flags, opt.state, ws
+        return plan
+
+    def run(self, opt) -> int:
+        if opt._kernel_flags != self.flags or opt.state is not self.state:
+            return -1
+        return self.ext.plan_step(self.cap)
+
+
+_HOST_EXT = None
+_PLAN_MAX_MISSES = 8
+
+
+def _host_ext():
+    """The _smo_host extension (built in-tree by smo_optimizer_b200.build)."""
+    global _HOST_EXT
+    if _HOST_EXT is None:
+        try:
+            from . import _smo_host
+        except ImportError as e:
+            raise _lib.SmoError("host extension _smo_host not built (run `python -m smo_optimizer_b200.build`)") \
+                from e
+        if _smo_host.sizeof_smo_tensor != _lib.TENSOR_DTYPE.itemsize:
+            raise _lib.SmoError("_smo_host was built against another smo_tensor layout")
+        _HOST_EXT = _smo_host
+    return _HOST_EXT
+
+
 def _named(params):
     params = list(params)
     if params and isinstance(params[0], tuple) and len(params[0]) == 2 and isinstance(params[0][0], str):
@@ -114,7 +206,7 @@ class _SpatialBase(Optimizer):
             params = protected_param_groups(_named(params), protect_output, quant_capable=self._quant)
         super().__init__(params, defaults)
         self.compress_conv = bool(compress_conv)
-        self._spare = {}        # param -> alternate moment buffers (double buffering)
+        self._spare = {}        # param -> (buffer set A, buffer set B) of double-buffered moments
         self._workspace = {}    # device index -> uint8 workspace tensor
         self._hyper_cache = {}
         self._inv_perm = {}     # param -> (row_perm, col_perm, their inverses) for permute_basis
@@ -122,6 +214,11 @@ class _SpatialBase(Optimizer):
         # smo_tensor.flags for every tensor (SMO_FLAG_GENERAL_PATH pins the
         # general two-launch kernels; used to cross-check the fused kernel)
         self._kernel_flags = 0
+        # step plan of the C++ host path (_smo_host); built after a step of the
+        # Python path, dropped when it stops applying (_PLAN_MAX_MISSES misses
+        # with no plan step in between turn it off until the state is loaded)
+        self._plan = None
+        self._plan_misses = 0
 
     # ---------------------------------------------------------------- state
 
@@ -144,6 +241,8 @@ class _SpatialBase(Optimizer):
         self._spare.clear()
         self._inv_perm.clear()
         self._rows.clear()
+        self._plan = None
+        self._plan_misses = 0
 
     def _hyper(self, group, step):
         return self._hyper_words(group, step)[0]
@@ -178,6 +277,17 @@ class _SpatialBase(Optimizer):
             with torch.enable_grad():
                 loss = closure()
 
+        plan = self._plan
+        if plan is not None:
+            rc = plan.run(self)
+            if rc == 0:
+                self._plan_misses = 0
+                return loss
+            if rc > 0:
+                _lib.check(rc, "smo_step")
+            self._plan = None
+            self._plan_misses += 1
+
         per_dev = {}
         for group in self.param_groups:
             for p in group["params"]:
@@ -201,34 +311,62 @@ class _SpatialBase(Optimizer):
 
         for dev, items in per_dev.items():
             self._launch(dev, items)
+        if self._plan_misses < _PLAN_MAX_MISSES:
+            self._plan = _StepPlan.build(self)
         return loss
+
+    # ---------------------------------------------------------------- buffers
+
+    # (state keys of the moments, double-buffered?) of a tensor's state
+    def _moment_keys(self, state):
+        if "m_q" in state:
+            return ("m_q", "m_s", "v_q", "v_s"), bool(state.get("is_compressed"))
+        return ("exp_avg", "exp_avg_sq"), bool(state.get("is_compressed"))
+
+    def _other(self, p, state, keys):
+        """The buffer set a step of a double-buffered tensor writes: the one of
+        its pair that the state does not hold (a pair is made, with fresh
+        buffers, when the state holds neither)."""
+        cur = tuple(state[k] for k in keys)
+        pair = self._spare.get(p)
+        if pair is not None:
+            a, b = pair
+            if all(x is y for x, y in zip(cur, a)):
+                return b
+            if all(x is y for x, y in zip(cur, b)):
+                return a
+        spare = tuple(torch.empty_like(t) for t in cur)
+        self._spare[p] = (cur, spare)
+        return spare
+
+    def _swap(self, p, state):
+        keys, double = self._moment_keys(state)
+        if double:
+            state.update(zip(keys, self._other(p, state, keys)))
 
     def _check_compress(self, group):
         pass
 
     # Descriptor rows: the first time a tensor is seen with a given set of
     # buffers, _fill writes its row field by field; the finished row is kept
-    # (keyed by the parameter's and the current moment buffer's addresses, the
-    # group and the kernel flags, so the two ping-pong parities get one row
-    # each) and later steps only patch the gradient address and the step's
-    # scalars.
+    # (keyed by every address it holds, the group and the kernel flags, so the
+    # two ping-pong parities get one row each) and later steps only patch the
+    # gradient address and the step's scalars.
     _ROW_WORDS = _lib.TENSOR_DTYPE.itemsize // 8
     _GRAD_WORD = _lib.TENSOR_DTYPE.fields["grad"][1] // 8
     _HP_WORD = _lib.TENSOR_DTYPE.fields["hp"][1] // 8
     _HP_WORDS = _lib.HYPER_DTYPE.itemsize // 8
 
-    @staticmethod
-    def _moment_ptr(state):
-        t = state.get("m_q")
-        if t is None:
-            t = state.get("exp_avg")
-        return t.data_ptr() if t is not None else 0
-
     def _row(self, p, grad, state, group):
-        perm = state.get("row_perm")
-        key = (p.data_ptr(), self._moment_ptr(state), id(group), self._kernel_flags,
-               getattr(self, "low_peak", False), getattr(self, "band_mb", 0.0),
-               perm.data_ptr() if perm is not None else 0)
+        # every address the row encodes is part of its key: the parameter, the
+        # moment buffers read and written, the basis permutations
+        keys, double = self._moment_keys(state)
+        ptrs = tuple(state[k].data_ptr() for k in keys)
+        if double:
+            ptrs += tuple(t.data_ptr() for t in self._other(p, state, keys))
+        perm = (state["row_perm"].data_ptr(), state["col_perm"].data_ptr()) if "row_perm" in state else ()
+        key = (p.data_ptr(), ptrs, perm, id(group), self._kernel_flags, getattr(self, "low_peak", False),
+               getattr(self, "band_mb", 0.0))
         rows = self._rows.get(p)
         if rows is None:
             rows = self._rows[p] = {}
@@ -306,9 +444,6 @@ class _SpatialBase(Optimizer):
                 dst.copy_(src)
         for p, grad, state, group in items:
             self._swap(p, state)
-
-    def _swap(self, p, state):
-        pass
 
     def workspace_status(self) -> int:
         """Device-side status of the steps since the last check, on every device
@@ -451,12 +586,6 @@ class SMO8bit(_SpatialBase):
             self._inv_perm[p] = cached
         return cached
 
-    def _spares(self, p, state):
-        sp = self._spare.get(p)
-        if sp is None or sp[0].shape != state["m_q"].shape:
-            sp = tuple(torch.empty_like(state[k]) for k in ("m_q", "m_s", "v_q", "v_s"))
-            self._spare[p] = sp
-        return sp
 
     def _fill(self, rec, p, grad, state, group):
         _check_state(p, state, self._STATE_DTYPES + tuple((k, p.dtype) for k in self._PARAM_DTYPE_STATE))
@@ -484,7 +613,7 @@ class SMO8bit(_SpatialBase):
             if "row_perm" in state:
                 for k, t in zip(("row_perm", "col_perm", "row_perm_inv", "col_perm_inv"), self._perms(p, state)):
                     rec[k] = t.data_ptr()
-            sp = self._spares(p, state)
+            sp = self._other(p, state, ("m_q", "m_s", "v_q", "v_s"))
             for k, s in zip(("m_q", "m_s", "v_q", "v_s"), sp):
                 rec[k + "_in"] = state[k].data_ptr()
                 rec[k + "_out"] = s.data_ptr()
@@ -495,14 +624,6 @@ class SMO8bit(_SpatialBase):
             rec["rows"], rec["cols"] = p.numel(), 1
             rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()
             rec["v_in"] = rec["v_out"] = state["exp_avg_sq"].data_ptr()
-
-    def _swap(self, p, state):
-        if state.get("is_compressed"):
-            sp = self._spare[p]
-            old = tuple(state[k] for k in ("m_q", "m_s", "v_q", "v_s"))
-            for k, s in zip(("m_q", "m_s", "v_q", "v_s"), sp):
-                state[k] = s
-            self._spare[p] = old
 
 
 class SMO(_SpatialBase):
@@ -572,10 +693,7 @@ class SMO(_SpatialBase):
             rec["kind"] = _lib.SMO_KIND_POOLED32
             rec["rows"], rec["cols"] = state["orig_shape"]
             rec["comp_rows"], rec["comp_cols"] = state["exp_avg"].shape
-            sp = self._spare.get(p)
-            if sp is None or sp[0].shape != state["exp_avg"].shape:
-                sp = (torch.empty_like(state["exp_avg"]), torch.empty_like(state["exp_avg_sq"]))
-                self._spare[p] = sp
+            sp = self._other(p, state, ("exp_avg", "exp_avg_sq"))
             rec["m_in"], rec["v_in"] = state["exp_avg"].data_ptr(), state["exp_avg_sq"].data_ptr()
             rec["m_out"], rec["v_out"] = sp[0].data_ptr(), sp[1].data_ptr()
         else:
@@ -586,9 +704,3 @@ class SMO(_SpatialBase):
             rec["m_in"] = rec["m_out"] = state["exp_avg"].data_ptr()
             rec["v_in"] = rec["v_out"] = state["exp_avg_sq"].data_ptr()
 
-    def _swap(self, p, state):
-        if state.get("is_compressed"):
-            sp = self._spare[p]
-            old = (state["exp_avg"], state["exp_avg_sq"])
-            state["exp_avg"], state["exp_avg_sq"] = sp
-            self._spare[p] = old

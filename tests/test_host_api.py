@@ -194,6 +194,27 @@ def test_step_scalars_follow_python_double_arithmetic():
     assert _host.step_scalars(1e-3, (0.9, 0.999), 1e-8, 0, 1).wd_on == 0
 
 
+def test_host_extension_forms_the_scalars_as_the_python_path():
+    """The C++ host path (_smo_host) forms each step's fp32 scalars from the
+    group's Python numbers exactly as _host.step_scalars does (double
+    arithmetic, one rounding), for steps 1 .. 10^6 and assorted values."""
+    from smo_optimizer_b200 import optimizers
+    ext = optimizers._host_ext()
+    assert ext.sizeof_smo_tensor == _lib.TENSOR_DTYPE.itemsize
+    rng = np.random.default_rng(0)
+    cases = [(1e-3, 0.9, 0.999, 1e-8, 0.01), (3e-4, 0.8, 0.99, 1e-6, 0), (1, 0.5, 0.5, 1e-12, 1e-5),
+             (2e-3, 0.0, 0.0, 0.0, 0.1)]
+    cases += [tuple(float(x) for x in (10 ** rng.uniform(-6, -1), rng.uniform(0, 0.999), rng.uniform(0.9, 0.99999),
+                                       10 ** rng.uniform(-12, -4), rng.uniform(0, 0.2))) for _ in range(40)]
+    steps = [1, 2, 3, 7, 10, 100, 1000, 12345, 10 ** 6]
+    for lr, b1, b2, eps, wd in cases:
+        for step in steps:
+            s = _host.step_scalars(lr, (b1, b2), eps, wd, step)
+            want = np.array([(s.beta1, s.omb1, s.beta2, s.omb2, s.wd, s.wd_on, s.neg_step, s.sqrt_bc2, s.eps, 0)],
+                            dtype=_lib.HYPER_DTYPE).tobytes()
+            assert ext.hyper_bytes(lr, b1, b2, eps, wd, step) == want, (lr, b1, b2, eps, wd, step)
+
+
 @pytest.mark.parametrize("cls", [SMO, SMO8bit])
 def test_constructor_errors(cls):
     p = [torch.nn.Parameter(torch.zeros(32, 32))]
