@@ -312,7 +312,7 @@ def run_reference(args, rank, world):
         return 0
     from smo_optimizer_b200 import workloads
 
-    wl = workloads.WORKLOADS[args.workload]
+    wl = workloads.get(args.workload)
     n = len(wl.tensors)
     classes, why = import_reference()
     budget = float(os.environ.get("SMO_REFERENCE_BUDGET_S", "120"))
@@ -422,7 +422,7 @@ def main():
     device = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
-    wl = workloads.WORKLOADS[args.workload]
+    wl = workloads.get(args.workload)
     cls = SMO8bit if wl.optimizer == "SMO8bit" else SMO
     kw = dict(wl.kwargs)
 

@@ -103,3 +103,17 @@ WORKLOADS = {
     "decoder700m_4layers": Workload("decoder700m_4layers", _decoder700m_tensors()[:16], "SMO8bit",
                                     dict(_HP, k_ratio=0.25, block_size=64, low_peak=True)),
 }
+
+
+def get(name: str) -> Workload:
+    """A named workload, or ``RxCxN``: N tensors of R x C with the 700M
+    decoder's optimizer settings (a single-shape set, for per-shape
+    measurements)."""
+    if name in WORKLOADS:
+        return WORKLOADS[name]
+    parts = name.split("x")
+    if len(parts) == 3 and all(x.isdigit() and int(x) > 0 for x in parts):
+        r, c, n = map(int, parts)
+        base = WORKLOADS["decoder700m"]
+        return Workload(name, tuple((f"w{i}", (r, c)) for i in range(n)), base.optimizer, base.kwargs)
+    raise KeyError(f"unknown workload {name!r}: one of {sorted(WORKLOADS)} or RxCxN")
