@@ -45,6 +45,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="decoder700m")
+    ap.add_argument("--dtype", default="f32", choices=sorted(DTYPES),
+                    help="parameter and gradient dtype (the reference steps half-precision parameters in their dtype)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--e2e-chunks", type=int, default=24)
@@ -131,22 +133,27 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
-def build_workload(wl, seed, device, owned):
-    """Params (all tensors) and grads (owned tensors) filled on the device by the synthetic generator."""
+DTYPES = {"f32": "float32", "bf16": "bfloat16", "f16": "float16"}
+
+
+def build_workload(wl, seed, device, owned, dtype="f32"):
+    """Params (all tensors) and grads (owned tensors) filled on the device by
+    the synthetic generator (fp32 draws, rounded to ``dtype``)."""
     import torch
     from smo_optimizer_b200 import ops, synthetic
 
+    tdt = getattr(torch, DTYPES[dtype])
     params, grads = [], []
     for i, (name, shape) in enumerate(wl.tensors):
         p = torch.empty(shape, dtype=torch.float32, device=device)
         ops.synth_normal_(p, seed, synthetic.stream_id(synthetic.STREAM_PARAM, 0, i), 0.02)
-        params.append(torch.nn.Parameter(p))
+        params.append(torch.nn.Parameter(p.to(tdt) if tdt != torch.float32 else p))
         if owned[i]:
             g = torch.empty(shape, dtype=torch.float32, device=device)
             ops.synth_normal_(g, seed, synthetic.stream_id(synthetic.STREAM_GRAD, 1, i), 1e-3)
             if wl.bf16_grads:
                 g = g.to(torch.bfloat16).to(torch.float32)
-            params[-1].grad = g
+            params[-1].grad = g.to(tdt) if tdt != torch.float32 else g
         grads.append(params[-1].grad)
     return params, grads
 
@@ -388,12 +395,15 @@ def run_reference(args, rank, world):
     return 0
 
 
-def _config(wl, world):
-    gb = 8 * wl.numel / 1e9  # fp32 params and grads
+def _config(wl, world, dtype="f32"):
+    gb = (8 if dtype == "f32" else 4) * wl.numel / 1e9  # params and grads
     l2 = (f"inputs ({gb:.1f} GB of params and grads) larger than L2; no flush" if gb > 0.5 else
           f"inputs ({gb * 1e3:.0f} MB) fit in L2: a step re-reads what the previous step left there")
-    return {"workload": wl.name, "params": wl.numel, "tensors": len(wl.tensors),
-            "parallelism": f"zero1-dp{world}" if world > 1 else "single", **_cfg(wl), "l2": l2}
+    cfg = {"workload": wl.name, "params": wl.numel, "tensors": len(wl.tensors),
+           "parallelism": f"zero1-dp{world}" if world > 1 else "single", **_cfg(wl), "l2": l2}
+    if dtype != "f32":
+        cfg["param_dtype"] = dtype
+    return cfg
 
 
 def _cfg(wl):
@@ -427,7 +437,9 @@ def main():
     kw = dict(wl.kwargs)
 
     shapes = [s for _, s in wl.tensors]
-    costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64)) for s in shapes]
+    elem = 4 if args.dtype == "f32" else 2
+    costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64), elem=elem)
+             for s in shapes]
     shard_of = args.shard_of if world == 1 and args.shard_of > 1 else 0
     if shard_of:
         # one rank's share of a ZeRO-1 split, stepped alone on this GPU
@@ -439,7 +451,7 @@ def main():
     # N > 1: every rank holds every gradient (a replicated model's backward), which
     # the gradient reduce-scatter timing below needs; the local step reads only
     # the owned ones
-    params, grads = build_workload(wl, args.seed, device, owned if world == 1 else [True] * len(owned))
+    params, grads = build_workload(wl, args.seed, device, owned if world == 1 else [True] * len(owned), args.dtype)
     flat = None
     if world > 1:
         # ZeRO-1 layout: parameters rebound into one rank-contiguous buffer so the
@@ -518,7 +530,8 @@ def main():
     roof = {"bound": "hbm", "kernel": "smo step (all launches of one step)", "achieved": achieved,
             "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_src,
             "algorithmic_bytes_per_launch": my_bytes,
-            "traffic": load_traffic(wl.name, "step", shard_of or world, args.shard_rank if shard_of else rank)}
+            "traffic": load_traffic(wl.name if args.dtype == "f32" else f"{wl.name}:{args.dtype}", "step",
+                                    shard_of or world, args.shard_rank if shard_of else rank)}
 
     # ---- ZeRO-1 completion: one in-place all-gather of the flat parameter buffer
     zero1 = None
@@ -582,8 +595,8 @@ def main():
         idx = [i for i, o in enumerate(owned) if o]
         host_g = {i: grads[i].detach().cpu().pin_memory() for i in idx}
         host_p = {i: torch.empty(params[i].shape, dtype=params[i].dtype, pin_memory=True) for i in idx}
-        h2d = sum(host_g[i].numel() * 4 for i in idx)
-        d2h = sum(host_p[i].numel() * 4 for i in idx)
+        h2d = sum(host_g[i].numel() * host_g[i].element_size() for i in idx)
+        d2h = sum(host_p[i].numel() * host_p[i].element_size() for i in idx)
         n_chunks = min(len(idx), args.e2e_chunks)
         target = sum(params[i].numel() for i in idx) / max(n_chunks, 1)
         chunks, cur, acc = [], [], 0
@@ -657,7 +670,7 @@ def main():
                        "H2D, step and params D2H pipelined over chunks on three streams"}
 
     cpu = cpu_ref = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.dtype == "f32":
         cpu = cpu_baseline(wl, args.seed, args.cpu_sample_seconds)
         cpu_ref = reference_baseline(wl, args.seed, args.cpu_sample_seconds)
 
@@ -665,8 +678,8 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32+int8", "data": "synthetic (seeded counter-hash N(0,0.02) params, N(0,1e-3) grads)",
-            "config": dict(_config(wl, world), **({"shard": f"rank {args.shard_rank} of {shard_of}",
+            "dtype": f"{args.dtype}+int8", "data": "synthetic (seeded counter-hash N(0,0.02) params, N(0,1e-3) grads)",
+            "config": dict(_config(wl, world, args.dtype), **({"shard": f"rank {args.shard_rank} of {shard_of}",
                                                    "params": my_params} if shard_of else {})),
             "hbm_gbs": (my_bytes if shard_of else sum(costs)) / (ms_per_step * 1e-3) / 1e9,
             "kernel_ms_per_step": step_ms,

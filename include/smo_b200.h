@@ -90,7 +90,6 @@ typedef struct smo_hyper {
  *   DENSE      param/grad/m/v [rows] (cols = 1)
  *   QUANT_ONLY param/grad [rows] (cols = 1); codes/scales as POOLED8 over rows
  * Every non-code array holds elements of type `dtype` (fp32 for SMO_DTYPE_F32).
- * Half-precision tensors take the general two-launch kernels.
  */
 typedef struct smo_tensor {
     float *param;

@@ -64,17 +64,35 @@ def up_to_date() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB_PATH
-    tmp = LIB_PATH + ".tmp"
-    cmd = [nvcc_path(), *ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE, "-shared", "-o", tmp, *sources()]
+    import tempfile
+    from concurrent.futures import ThreadPoolExecutor
+
+    nvcc = nvcc_path()
+    flags = [*ARCH_FLAGS, *NVCC_FLAGS, "-I", INCLUDE]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
-        print(" ".join(cmd))
-    res = subprocess.run(cmd, capture_output=True, text=True)
-    if res.returncode != 0:
-        sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed to build libsmo_b200.so")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        flags.insert(0, "-Xptxas=-v")
+    with tempfile.TemporaryDirectory() as tmpdir:
+        # one nvcc per source file, in parallel, then one link
+        def compile_one(src):
+            obj = os.path.join(tmpdir, os.path.basename(src) + ".o")
+            cmd = [nvcc, *flags, "-c", src, "-o", obj]
+            if verbose:
+                print(" ".join(cmd))
+            return obj, subprocess.run(cmd, capture_output=True, text=True)
+
+        with ThreadPoolExecutor(max_workers=max(1, min(len(sources()), os.cpu_count() or 1))) as pool:
+            results = list(pool.map(compile_one, sources()))
+        for obj, res in results:
+            if verbose or res.returncode != 0:
+                sys.stderr.write(res.stdout + res.stderr)
+            if res.returncode != 0:
+                raise RuntimeError("nvcc failed to build libsmo_b200.so")
+        tmp = LIB_PATH + ".tmp"
+        res = subprocess.run([nvcc, *ARCH_FLAGS, "-shared", "-o", tmp, *[o for o, _ in results]],
+                             capture_output=True, text=True)
+        if res.returncode != 0:
+            sys.stderr.write(res.stdout + res.stderr)
+            raise RuntimeError("nvcc failed to link libsmo_b200.so")
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

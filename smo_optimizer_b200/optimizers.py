@@ -10,8 +10,7 @@ Differences a user can observe:
   * Tensors must live on a CUDA device; there is no CPU path.  Parameters
     are fp32, bf16 or fp16 with gradients of the same dtype; as in the
     reference, the state's block scales and float moments take the
-    parameter's dtype and every op rounds to it.  Half-precision tensors are
-    stepped by the general two-launch kernels (the fused kernel is fp32-only).
+    parameter's dtype and every op rounds to it.
   * Pooled moments are double-buffered: after a step ``state[p]['m_q']`` (and
     the other moment tensors) refer to the buffer the step wrote, and the
     previous buffer is reused two steps later.  ``state_dict()`` returns live

@@ -34,24 +34,26 @@ import torch.distributed as dist
 from . import _host
 
 
-def step_bytes(shape, kind: str, k_ratio: float = 0.25, block: int = 64, compress_conv: bool = False) -> int:
-    """Algorithmic HBM bytes of one tensor's step (what the kernels must move).
+def step_bytes(shape, kind: str, k_ratio: float = 0.25, block: int = 64, compress_conv: bool = False,
+               elem: int = 4) -> int:
+    """Algorithmic HBM bytes of one tensor's step (what the kernels must move),
+    for parameters of ``elem`` bytes (the state's floats have the same size).
 
-    pooled int8: p r+w, g r (12 B/elem) + codes r+w (4 B/cell) + scales r+w (16 B/block);
-    pooled fp32: 12 B/elem + 16 B/cell; dense fp32 Adam: 28 B/elem.
+    pooled int8: p r+w, g r (3 elem B/elem) + codes r+w (4 B/cell) + scales r+w (4 elem B/block);
+    pooled float: 3 elem B/elem + 4 elem B/cell; dense Adam: 7 elem B/elem.
     """
     n = 1
     for s in shape:
         n *= int(s)
     view = _host.compression_view(shape, compress_conv)
     if view is None:
-        return 28 * n
+        return 7 * elem * n
     h, w = _host.comp_shape(view[0], k_ratio)
     c = h * w
     if kind == "SMO8bit":
         qb = _host.pooled_q_block(view[1], (h, w), block)
-        return 12 * n + 4 * c + 16 * _host.num_blocks(c, qb)
-    return 12 * n + 16 * c
+        return 3 * elem * n + 4 * c + 4 * elem * _host.num_blocks(c, qb)
+    return 3 * elem * n + 4 * elem * c
 
 
 def lpt_partition(costs, world: int):

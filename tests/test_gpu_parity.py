@@ -233,7 +233,14 @@ def test_single1024_100_steps_bit_exact_vs_oracle():
 
 
 FUSED_CASES = ["single1024", "s8_128x256_mono", "s8_128x256_band", "s8_128x256_band_wd", "s8_multi",
-               "s8_132x2048_band", "s8_256x512_k0125", "smo_96x192_k05", "smo_groups"]
+               "s8_132x2048_band", "s8_256x512_k0125", "smo_96x192_k05", "smo_groups",
+               "bf16_s8_mono", "bf16_s8_band_groups", "bf16_smo", "fp16_s8_groups", "fp16_s8_band", "fp16_smo"]
+
+
+def bits(t):
+    """A tensor's bit patterns (NaN compares equal to the same NaN)."""
+    t = t.detach()
+    return t.view({4: torch.int32, 2: torch.int16, 1: torch.int8}[t.element_size()])
 
 
 @pytest.mark.parametrize("name", FUSED_CASES)
@@ -243,10 +250,44 @@ def test_fused_kernel_matches_general_kernels(name):
     fp, fs = run_gpu_case(name, steps=steps)
     gp, gs = run_gpu_case(name, steps=steps, general=True)
     for i, (a, b, sa, sb) in enumerate(zip(fp, gp, fs, gs)):
-        assert torch.equal(a, b), f"{name}[{i}] params differ between fused and general kernels"
+        assert torch.equal(bits(a), bits(b)), f"{name}[{i}] params differ between fused and general kernels"
         for k in C.STATE_ARRAY_KEYS:
             if k in sa:
-                assert torch.equal(sa[k], sb[k]), f"{name}[{i}] {k} differs between fused and general kernels"
+                assert torch.equal(bits(sa[k]), bits(sb[k])), \
+                    f"{name}[{i}] {k} differs between fused and general kernels"
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("H,W,k,block,band_mb,wd", [
+    (4 * 33, 4 * 300, 0.25, 64, 0.0, 0.01),     # blocks straddle rows
+    (4 * 40, 4 * 512, 0.25, 64, 0.25, 0.01),    # bands
+    (2 * 64, 2 * 640, 0.5, 64, 0.0, 0.0),       # 2x2 windows, two cells per thread
+    (8 * 24, 8 * 64, 0.125, 64, 0.0, 0.01),     # 8x8 windows (16-byte half rows)
+])
+def test_fused_half_precision_vs_oracle(dtype, H, W, k, block, band_mb, wd):
+    """bf16 / fp16 parameters through the fused kernel (every op rounded to
+    the dtype), bit-identical to the oracle over three steps."""
+    kw = dict(lr=2e-3, betas=(0.9, 0.99), eps=1e-8, weight_decay=wd, k_ratio=k, block_size=block)
+    if band_mb:
+        kw.update(low_peak=True, band_mb=band_mb)
+    std = 1e-3 if dtype == "bfloat16" else 0.05  # fp16: keep v above its underflow
+    p0 = C.round_to_dtype(synthetic.synth_normal(7, H, H * W, 0.02).reshape(H, W), dtype)
+    p = torch.nn.Parameter(cuda(p0, dtype))
+    opt = SMO8bit([p], **kw)
+    ref_p = p0.copy()
+    ref = oracle.OracleOptimizer("SMO8bit", [{"params": [ref_p]}], param_dtype=dtype, **kw)
+    for step in range(1, 4):
+        g = C.round_to_dtype(synthetic.synth_normal(8, step * 1000 + W, H * W, std).reshape(H, W), dtype)
+        p.grad = cuda(g, dtype)
+        opt.step()
+        ref.step([g])
+    torch.cuda.synchronize()
+    assert opt.workspace_status() == 0
+    st, rst = opt.state[p], ref.state[(0, 0)]
+    for key in ("m_q", "m_s", "v_q", "v_s"):
+        got = host(st[key]).reshape(-1)
+        assert np.array_equal(got, rst[key].reshape(-1), equal_nan=got.dtype != np.int8), key
+    assert np.array_equal(host(p), ref_p, equal_nan=True)
 
 
 @pytest.mark.parametrize("H,W,k,block,band_mb,wd", [
