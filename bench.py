@@ -411,6 +411,10 @@ def _cfg(wl):
     cfg = {"optimizer": wl.optimizer, "k_ratio": kw.get("k_ratio"), "block_size": kw.get("block_size"),
            "low_peak": kw.get("low_peak", False), "weight_decay": kw.get("weight_decay"),
            "protect_output": wl.protect_output, "bf16_grads": wl.bf16_grads}
+    if wl.compress is not True:
+        cfg["compress"] = wl.compress
+    if wl.general_path:
+        cfg["kernels"] = "general two-launch path pinned"
     return cfg
 
 
@@ -438,8 +442,8 @@ def main():
 
     shapes = [s for _, s in wl.tensors]
     elem = 4 if args.dtype == "f32" else 2
-    costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64), elem=elem)
-             for s in shapes]
+    costs = [zero.step_bytes(s, wl.optimizer, kw.get("k_ratio", 0.25), kw.get("block_size", 64), elem=elem,
+                             compress=wl.compress) for s in shapes]
     shard_of = args.shard_of if world == 1 and args.shard_of > 1 else 0
     if shard_of:
         # one rank's share of a ZeRO-1 split, stepped alone on this GPU
@@ -462,7 +466,9 @@ def main():
         named = [(n, p) for (n, _), p, o in zip(wl.tensors, params, owned) if o]
         opt = cls(named, protect_output=wl.protect_output, **kw)
     else:
-        opt = cls(mine, **kw)
+        opt = cls([{"params": mine, "compress": wl.compress}], **kw)
+    if wl.general_path:
+        opt._kernel_flags = _lib.SMO_FLAG_GENERAL_PATH
     my_params = sum(p.numel() for p in mine)
     my_bytes = sum(c for c, o in zip(costs, owned) if o)
     total_params = wl.numel
@@ -612,7 +618,10 @@ def main():
         def chunk_opt(members):
             if wl.protect_output:
                 return cls([(wl.tensors[i][0], params[i]) for i in members], protect_output=wl.protect_output, **kw)
-            return cls([params[i] for i in members], **kw)
+            o = cls([{"params": [params[i] for i in members], "compress": wl.compress}], **kw)
+            if wl.general_path:
+                o._kernel_flags = _lib.SMO_FLAG_GENERAL_PATH
+            return o
 
         opts = [chunk_opt(c) for c in chunks]
         s_in, s_comp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()

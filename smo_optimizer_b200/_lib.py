@@ -22,6 +22,7 @@ SMO_ERR_TIMEOUT = 5
 SMO_DTYPE_F32 = 0
 SMO_DTYPE_BF16 = 1
 SMO_DTYPE_F16 = 2
+SMO_FLAG_GENERAL_PATH = 1
 ABI_VERSION = 3
 
 # Field layout of struct smo_hyper / smo_tensor, as a numpy structured dtype so

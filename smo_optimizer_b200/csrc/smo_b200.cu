@@ -107,6 +107,10 @@ __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
     }
 }
 
+// quant_only: one int8 block of B elements per warp, in two passes (the
+// absmax, then the write; the second re-reads g, p and the codes, from L1 or
+// L2).  Keeping the elements in registers between the passes was measured
+// slower: the registers cost occupancy, and the kernel serves every kind.
 template <class T>
 __device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t N = d.H;
@@ -150,6 +154,12 @@ __device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
     }
 }
 
+// dense Adam moments: 1024 elements per warp.  Each lane takes groups of
+// four consecutive elements (16-byte fp32 / 8-byte half vector accesses when
+// all six arrays are aligned for them: four independent loads in flight per
+// lane); a group's loads come before its stores, so in-place moments
+// (in == out) are fine.  One group per iteration keeps the kernel, which
+// serves every kind, at its register budget.
 template <class T>
 __device__ void dense_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t N = d.H;
@@ -158,7 +168,32 @@ __device__ void dense_item(const DevDesc &d, int64_t item, int lane) {
     const smo_hyper &hp = d.hp;
     const T *g = (const T *)d.g, *m_in = (const T *)d.m_in, *v_in = (const T *)d.v_in;
     T *p = (T *)d.p, *m_out = (T *)d.m_out, *v_out = (T *)d.v_out;
-    for (int64_t i = base + lane; i < end; i += 32) {
+    constexpr uintptr_t kVec = 4 * sizeof(T);
+    const bool vec = (((uintptr_t)(g + base) | (uintptr_t)(p + base) | (uintptr_t)(m_in + base) |
+                       (uintptr_t)(v_in + base) | (uintptr_t)(m_out + base) | (uintptr_t)(v_out + base)) % kVec) == 0;
+    int64_t i0 = base;
+    if (vec) {
+        const int64_t vend = base + (end - base) / 4 * 4;  // end of the whole groups of four
+        for (int64_t i = base + 4 * lane; i < vend; i += 4 * 32) {
+            float pv[4], gv[4], mv[4], vv[4];
+            ld4<T>(p + i, pv);
+            ld4<T>(g + i, gv);
+            ld4<T>(m_in + i, mv);
+            ld4<T>(v_in + i, vv);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float x = decayed<T>(gv[k], pv[k], hp);
+                mv[k] = ema<T>(mv[k], x, hp.beta1, hp.omb1);
+                vv[k] = ema_sq<T>(vv[k], x, hp.beta2, hp.omb2);
+                pv[k] = adam_write<T>(pv[k], mv[k], vv[k], hp);
+            }
+            st4<T>(m_out + i, mv);
+            st4<T>(v_out + i, vv);
+            st4<T>(p + i, pv);
+        }
+        i0 = vend;
+    }
+    for (int64_t i = i0 + lane; i < end; i += 32) {
         float pi = ld<T>(p + i);
         float x = decayed<T>(ld<T>(g + i), pi, hp);
         float m = ema<T>(ld<T>(m_in + i), x, hp.beta1, hp.omb1);

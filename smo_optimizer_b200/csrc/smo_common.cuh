@@ -46,6 +46,34 @@ __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16 *p, float x) { *
 template <>
 __device__ __forceinline__ void st<__half>(__half *p, float x) { *p = __float2half_rn(x); }
 
+// Four consecutive elements (one 16-byte fp32 or 8-byte half access; the
+// address must be aligned to that size) as fp32, and back.
+template <class T>
+__device__ __forceinline__ void ld4(const T *p, float (&v)[4]) {
+    if constexpr (sizeof(T) == 4) {
+        const float4 t = *reinterpret_cast<const float4 *>(p);
+        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
+    } else {
+        const uint2 t = *reinterpret_cast<const uint2 *>(p);
+        const T *e = reinterpret_cast<const T *>(&t);
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = ld<T>(e + k);
+    }
+}
+
+template <class T>
+__device__ __forceinline__ void st4(T *p, const float (&v)[4]) {
+    if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4 *>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+        uint2 t;
+        T *e = reinterpret_cast<T *>(&t);
+#pragma unroll
+        for (int k = 0; k < 4; k++) st<T>(e + k, v[k]);
+        *reinterpret_cast<uint2 *>(p) = t;
+    }
+}
+
 // ---------------------------------------------------------------- scalars
 
 // x = g + wd * p  (grad.add(p, alpha=wd), spatial_8bit.py:217-218)

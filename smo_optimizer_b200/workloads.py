@@ -20,6 +20,8 @@ class Workload:
     kwargs: dict = field(default_factory=dict)
     protect_output: object = False
     bf16_grads: bool = False
+    compress: object = True      # the group's compress setting (True, False = dense, "quant_only")
+    general_path: bool = False   # pin the general two-launch kernels (SMO_FLAG_GENERAL_PATH)
 
     @property
     def numel(self) -> int:
@@ -105,15 +107,24 @@ WORKLOADS = {
 }
 
 
+_MODES = {"": {}, "dense": dict(compress=False), "quant_only": dict(compress="quant_only"),
+          "general": dict(general_path=True)}
+
+
 def get(name: str) -> Workload:
-    """A named workload, or ``RxCxN``: N tensors of R x C with the 700M
+    """A named workload, or ``RxCxN[@mode]``: N tensors of R x C with the 700M
     decoder's optimizer settings (a single-shape set, for per-shape
-    measurements)."""
+    measurements); ``@dense`` / ``@quant_only`` put them in a group with that
+    ``compress`` setting, ``@general`` pins the general two-launch kernels."""
     if name in WORKLOADS:
         return WORKLOADS[name]
-    parts = name.split("x")
-    if len(parts) == 3 and all(x.isdigit() and int(x) > 0 for x in parts):
+    shape, _, mode = name.partition("@")
+    parts = shape.split("x")
+    if len(parts) == 3 and all(x.isdigit() and int(x) > 0 for x in parts) and mode in _MODES:
         r, c, n = map(int, parts)
         base = WORKLOADS["decoder700m"]
-        return Workload(name, tuple((f"w{i}", (r, c)) for i in range(n)), base.optimizer, base.kwargs)
-    raise KeyError(f"unknown workload {name!r}: one of {sorted(WORKLOADS)} or RxCxN")
+        kwargs = dict(base.kwargs)
+        if mode in ("dense", "quant_only"):
+            kwargs.pop("low_peak", None)
+        return Workload(name, tuple((f"w{i}", (r, c)) for i in range(n)), base.optimizer, kwargs, **_MODES[mode])
+    raise KeyError(f"unknown workload {name!r}: one of {sorted(WORKLOADS)} or RxCxN[@dense|@quant_only|@general]")

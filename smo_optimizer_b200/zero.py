@@ -35,17 +35,22 @@ from . import _host
 
 
 def step_bytes(shape, kind: str, k_ratio: float = 0.25, block: int = 64, compress_conv: bool = False,
-               elem: int = 4) -> int:
+               elem: int = 4, compress=True) -> int:
     """Algorithmic HBM bytes of one tensor's step (what the kernels must move),
-    for parameters of ``elem`` bytes (the state's floats have the same size).
+    for parameters of ``elem`` bytes (the state's floats have the same size)
+    in a group with the given ``compress`` setting.
 
     pooled int8: p r+w, g r (3 elem B/elem) + codes r+w (4 B/cell) + scales r+w (4 elem B/block);
-    pooled float: 3 elem B/elem + 4 elem B/cell; dense Adam: 7 elem B/elem.
+    pooled float: 3 elem B/elem + 4 elem B/cell; dense Adam: 7 elem B/elem;
+    quant_only: 3 elem B/elem + codes r+w (4 B/elem) + scales r+w (4 elem B/block).
     """
     n = 1
     for s in shape:
         n *= int(s)
-    view = _host.compression_view(shape, compress_conv)
+    if compress == "quant_only":
+        qb = _host.quant_only_q_block(shape, block)
+        return 3 * elem * n + 4 * n + 4 * elem * _host.num_blocks(n, qb)
+    view = _host.compression_view(shape, compress_conv) if compress else None
     if view is None:
         return 7 * elem * n
     h, w = _host.comp_shape(view[0], k_ratio)
