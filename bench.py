@@ -506,10 +506,11 @@ def main():
         opt.step()
         host_t.append(time.perf_counter() - h0)
         ev[k][1].record(stream)
+    t_end.record(stream)
     # host time of one step() call: the median of the first ten (launches are
     # asynchronous; later calls of a long run can wait for room in the launch queue)
     host_ms = float(np.median(host_t[:10])) * 1e3
-    t_end.record(stream)
+    host_ms_max = float(np.max(host_t)) * 1e3
     torch.cuda.synchronize()
     launches = lib.smo_launch_count() - launches0
     barrier()
@@ -693,6 +694,7 @@ def main():
             "hbm_gbs": (my_bytes if shard_of else sum(costs)) / (ms_per_step * 1e-3) / 1e9,
             "kernel_ms_per_step": step_ms,
             "host_ms_per_step": host_ms,
+            "host_ms_max": host_ms_max,
             "roofline": roof,
             "cpu_baseline": cpu_ref or cpu,
             "cpu_baseline_port": cpu,

@@ -228,13 +228,17 @@ __global__ void __launch_bounds__(256) step_a_kernel(const __grid_constant__ Bat
 // scratch for POOLED8, the state's type T for POOLED32), parameter of type T.
 template <class T, class S>
 __device__ __forceinline__ void adam_row(const DevDesc &d, int64_t r, int lane) {
-    const S *mo = (const S *)d.m_out, *vo = (const S *)d.v_out;
+    // the moments (scratch or the new state) and the parameter never overlap
+    const S *__restrict__ mo = (const S *)d.m_out;
+    const S *__restrict__ vo = (const S *)d.v_out;
     // permute_basis: parameter row r / column q sit at row rpi[r] / column
     // cpi[q] of the basis the moments were reconstructed in
     const int64_t br = d.rpi ? d.rpi[r] : r;
     int small;
     const Coef rc = row_coef(br, d.H, d.h, d.W, d.band, small);
-    T *prow = (T *)d.p + r * d.W;
+    T *__restrict__ prow = (T *)d.p + r * d.W;
+    const float cscale = d.w == d.W ? 1.0f : coef_scale(d.w, d.W);  // the same for every column
+#pragma unroll 2
     for (int64_t q = lane; q < d.W; q += 32) {
         const int64_t bq = d.cpi ? d.cpi[q] : q;
         float mh, vh;
@@ -242,7 +246,7 @@ __device__ __forceinline__ void adam_row(const DevDesc &d, int64_t r, int lane) 
             mh = ld<S>(mo + br * d.w + bq);
             vh = ld<S>(vo + br * d.w + bq);
         } else {
-            const Coef cc = coef_for(bq, d.w, d.W);
+            const Coef cc = coef_for_scaled(bq, d.w, d.W, cscale);
             if (small) {
                 mh = interp_small<S>(mo, d.w, rc, cc);
                 vh = interp_small<S>(vo, d.w, rc, cc);

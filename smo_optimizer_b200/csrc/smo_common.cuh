@@ -216,7 +216,12 @@ struct Coef {
     int ident;  // equal extents: pass-through
 };
 
-__device__ __forceinline__ Coef coef_for(int64_t o, int64_t in, int64_t out) {
+// torch's source-index scale in / out of one interpolated dimension
+__device__ __forceinline__ float coef_scale(int64_t in, int64_t out) { return __fdiv_rn((float)in, (float)out); }
+
+// coefficients of output index o, with scale = coef_scale(in, out) (callers
+// that walk a whole row form it once)
+__device__ __forceinline__ Coef coef_for_scaled(int64_t o, int64_t in, int64_t out, float scale) {
     Coef c;
     if (in == out) {
         c.i0 = c.i1 = o;
@@ -225,7 +230,6 @@ __device__ __forceinline__ Coef coef_for(int64_t o, int64_t in, int64_t out) {
         c.ident = 1;
         return c;
     }
-    float scale = __fdiv_rn((float)in, (float)out);
     float real = __fmaf_rn(scale, __fadd_rn((float)o, 0.5f), -0.5f);
     real = real < 0.0f ? 0.0f : real;
     int64_t i0 = (int64_t)floorf(real);
@@ -238,6 +242,10 @@ __device__ __forceinline__ Coef coef_for(int64_t o, int64_t in, int64_t out) {
     c.l0 = __fsub_rn(1.0f, l1);
     c.ident = 0;
     return c;
+}
+
+__device__ __forceinline__ Coef coef_for(int64_t o, int64_t in, int64_t out) {
+    return coef_for_scaled(o, in, out, in == out ? 1.0f : coef_scale(in, out));
 }
 
 // Row coefficients; interp_band > 0 reproduces the low_peak bands of
