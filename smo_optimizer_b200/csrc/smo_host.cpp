@@ -6,8 +6,8 @@
 // one call, plan_step(), which
 //   1. checks that nothing the plan relies on has changed: the param groups
 //      and their parameter lists (identity), each parameter's data pointer
-//      and gradient (defined, strided, same dtype and device, the layout the
-//      descriptor assumes), the state's moment tensors (one of the two buffer
+//      and layout, its gradient (defined, strided, same dtype and device, the
+//      layout the descriptor assumes), the state's moment tensors (one of the two buffer
 //      sets), its integer "step", and no change to the optimizer's state
 //      mapping (a dict watcher);
 //   2. increments each state's "step", writes the gradient pointer and the
@@ -58,6 +58,7 @@ struct Entry {
     PyObject *set[2][4] = {};   // owned: buffer set 0 (the state's at plan time) and set 1
     smo_tensor row[2];          // descriptor while the state holds set 0 / set 1
     void *param_ptr = nullptr;
+    std::vector<int64_t> sizes, strides;  // the parameter's layout the rows were made for
     bool dense = false;         // gradient must have the parameter's sizes and strides (else contiguous)
 };
 
@@ -182,6 +183,7 @@ int run_plan(Plan &pl) {
             continue;
         }
         if (!g.defined() || pt.data_ptr() != e.param_ptr) return -1;
+        if (pt.sizes() != c10::IntArrayRef(e.sizes) || pt.strides() != c10::IntArrayRef(e.strides)) return -1;
         if (g.layout() != c10::kStrided || g.scalar_type() != pt.scalar_type() || g.device() != pt.device())
             return -1;
         if (g.sizes() != pt.sizes()) return -1;
@@ -312,7 +314,12 @@ PyObject *plan_new(PyObject *, PyObject *args) {
         e.param = PyTuple_GET_ITEM(t, 0);
         Py_INCREF(e.param);
         if (!THPVariable_Check(e.param)) goto bad_structure;
-        e.param_ptr = THPVariable_Unpack(e.param).data_ptr();
+        {
+            const at::Tensor &pt = THPVariable_Unpack(e.param);
+            e.param_ptr = pt.data_ptr();
+            e.sizes.assign(pt.sizes().begin(), pt.sizes().end());
+            e.strides.assign(pt.strides().begin(), pt.strides().end());
+        }
         PyObject *state = PyTuple_GET_ITEM(t, 1);
         if (state == Py_None) continue;
         if (PyTuple_GET_SIZE(t) != 10 || !PyDict_Check(state)) goto bad_structure;
