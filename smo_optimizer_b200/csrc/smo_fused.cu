@@ -103,9 +103,13 @@ static int window_key(const smo_tensor &t) {
 }
 
 // CTA width of a launch: 192 threads (four CTAs of 80 registers per SM, so
-// four independent row pipelines hide each other's load latency), or 256 when
-// that leaves fewer idle thread-columns over the batch's compact rows (a
-// compact row of w cells takes ceil(w / NT) passes of NT threads).
+// four independent row pipelines hide each other's load latency), or 256 or
+// 128 (six CTAs per SM) when that leaves fewer idle thread-columns over the
+// batch's compact rows (a compact row of w cells takes ceil(w / NT) passes of
+// NT threads); ties keep 192.  Narrow rows are where 128 wins: the TinyViT and
+// char-LM sets (rows of 96-512 cells) step 5-11 % faster with it, while the
+// 700M decoder's rows (384-1536 cells, no idle columns at 192) run 5-8 %
+// slower with it, whole or in per-rank shares.
 // SMO_B200_FUSED_THREADS (128, 192, 256 or 384) forces one width, for
 // measurements.
 int pick_threads(const FusedBatch &b) {
@@ -115,12 +119,14 @@ int pick_threads(const FusedBatch &b) {
         forced = e ? atoi(e) : 0;
     }
     if (forced == 128 || forced == 192 || forced == 256 || forced == 384) return forced;
-    int64_t idle192 = 0, idle256 = 0;
+    int64_t idle128 = 0, idle192 = 0, idle256 = 0;
     for (int i = 0; i < b.n; i++) {
         const int64_t w = b.d[i].w, rows = b.d[i].h;
+        idle128 += rows * ((w + 127) / 128 * 128 - w);
         idle192 += rows * ((w + 191) / 192 * 192 - w);
         idle256 += rows * ((w + 255) / 256 * 256 - w);
     }
+    if (idle128 < idle192 && idle128 < idle256) return 128;
     return idle256 < idle192 ? 256 : 192;
 }
 
