@@ -108,9 +108,11 @@ __device__ void pooled_block_item(const DevDesc &d, int64_t item, int lane) {
 }
 
 // quant_only: one int8 block of B elements per warp, in two passes (the
-// absmax, then the write; the second re-reads g, p and the codes, from L1 or
-// L2).  Keeping the elements in registers between the passes was measured
-// slower: the registers cost occupancy, and the kernel serves every kind.
+// absmax, then the write).  Blocks of up to 64 elements (the default) keep
+// their two elements per lane in registers between the passes; larger blocks
+// re-read g, p and the codes in the second pass (from L1 or L2).  Holding
+// more elements per lane was measured slower: the registers cost occupancy,
+// and the kernel serves every kind.
 template <class T>
 __device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
     const int64_t N = d.H;
@@ -122,6 +124,42 @@ __device__ void quant_only_item(const DevDesc &d, int64_t item, int lane) {
     const float tm = dequant_step<T>(ld<T>((const T *)d.ms_in + item));
     const float tv = dequant_step<T>(ld<T>((const T *)d.vs_in + item));
     float am = 0.0f, av = 0.0f;
+    if (B <= 64) {
+        float pr[2], mr[2], vr[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int64_t k = lane + 32 * u, i = base + k;
+            pr[u] = mr[u] = vr[u] = 0.0f;
+            if (k < B && i < N) {
+                pr[u] = ld<T>(p + i);
+                const float x = decayed<T>(ld<T>(g + i), pr[u], hp);
+                mr[u] = ema<T>(dequant1<T>(d.mq_in[i], tm), x, hp.beta1, hp.omb1);
+                vr[u] = ema_sq<T>(dequant1<T>(d.vq_in[i], tv), x, hp.beta2, hp.omb2);
+                am = absmax_acc(am, mr[u]);
+                av = absmax_acc(av, vr[u]);
+            }
+        }
+        const float sm = block_scale<T>(warp_absmax(am));
+        const float sv = block_scale<T>(warp_absmax(av));
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int64_t k = lane + 32 * u, i = base + k;
+            if (k >= B) break;
+            if (i < N) {
+                d.mq_out[i] = quantize1<T>(mr[u], sm);
+                d.vq_out[i] = quantize1<T>(vr[u], sv);
+                st<T>(p + i, adam_write<T>(pr[u], mr[u], vr[u], hp));
+            } else {
+                d.mq_out[i] = 0;
+                d.vq_out[i] = 0;
+            }
+        }
+        if (lane == 0) {
+            st<T>((T *)d.ms_out + item, sm);
+            st<T>((T *)d.vs_out + item, sv);
+        }
+        return;
+    }
     for (int64_t k = lane; k < B; k += 32) {
         int64_t i = base + k;
         if (i >= N) break;
