@@ -275,3 +275,23 @@ def test_protect_output_groups():
     assert len(opt.param_groups) == 2 and opt.param_groups[1]["compress"] is False
     with pytest.raises(ValueError):
         SMO8bit([p for _, p in named], protect_output=True)
+
+
+def test_single_shape_workload_names():
+    """bench.py's RxCxN[@mode] sets: N tensors of R x C with the decoder's
+    settings; the modes pick the group's compress setting or pin the general
+    kernels, and the algorithmic bytes follow the mode."""
+    from smo_optimizer_b200 import workloads, zero
+    wl = workloads.get("64x128x3")
+    assert wl.tensors == (("w0", (64, 128)), ("w1", (64, 128)), ("w2", (64, 128)))
+    assert wl.compress is True and not wl.general_path and wl.kwargs["low_peak"]
+    assert workloads.get("64x128x3@dense").compress is False
+    assert workloads.get("64x128x3@quant_only").compress == "quant_only"
+    assert workloads.get("64x128x3@general").general_path
+    for bad in ("64x128", "64x128x0", "64x128x3@fast", "nope"):
+        with pytest.raises(KeyError):
+            workloads.get(bad)
+    n = 64 * 128
+    assert zero.step_bytes((64, 128), "SMO8bit", compress=False) == 28 * n
+    assert zero.step_bytes((64, 128), "SMO8bit", compress="quant_only") == 16 * n + 16 * (n // 64)
+    assert zero.step_bytes((64, 128), "SMO8bit", elem=2) == 6 * n + 4 * (16 * 32) + 8 * (16 * 32 // 64)
