@@ -347,19 +347,39 @@ __device__ __forceinline__ float2 pool_cell(const float (&gv)[KH][KW], const flo
     return rd2<T>(__fmul2_rn(acc, splat(inv)));
 }
 
+// The old moments of a cell as loaded (codes and scales, or the fp32-kind
+// moments).  Phase 1 issues these loads together with the cell's g and p
+// loads, so that all of a cell's DRAM reads are in flight at once (4 % faster
+// on rows of 384 cells than loading them after the pooling).
+struct OldCell {
+    int qm, qv;
+    float a, b;
+};
+
+template <class T>
+__device__ __forceinline__ OldCell load_old(const FusedDesc &d, uint32_t cell) {
+    OldCell o;
+    if (d.kind == SMO_KIND_POOLED8) {
+        const uint32_t bl = fast_div(cell, d.div_B);
+        o.qm = d.mq_in[cell];
+        o.qv = d.vq_in[cell];
+        o.a = ld<T>((const T *)d.ms_in + bl);
+        o.b = ld<T>((const T *)d.vs_in + bl);
+    } else {
+        o.qm = o.qv = 0;
+        o.a = ld<T>((const T *)d.m_in + cell);
+        o.b = ld<T>((const T *)d.v_in + cell);
+    }
+    return o;
+}
+
 // dequant of the old moments, EMA, post-EMA pair into the ring row (the
 // ring holds fp32 values; for T = bf16 / fp16 they are values of T)
 template <class T>
-__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, float2 pooled, float2 *row, int j,
-                                         bool own) {
+__device__ __forceinline__ void ema_cell(const FusedDesc &d, uint32_t cell, const OldCell &o, float2 pooled,
+                                         float2 *row, int j, bool own) {
     const smo_hyper &hp = d.hp;
-    float2 mv;
-    if (d.kind == SMO_KIND_POOLED8) {
-        const uint32_t b = fast_div(cell, d.div_B);
-        mv = dequant2<T>(d.mq_in[cell], d.vq_in[cell], ld<T>((const T *)d.ms_in + b), ld<T>((const T *)d.vs_in + b));
-    } else {
-        mv = f2(ld<T>((const T *)d.m_in + cell), ld<T>((const T *)d.v_in + cell));
-    }
+    float2 mv = d.kind == SMO_KIND_POOLED8 ? dequant2<T>((int8_t)o.qm, (int8_t)o.qv, o.a, o.b) : f2(o.a, o.b);
     // m.mul_(beta).add_(u, alpha=1-beta): alpha rounded to T, each op rounded
     mv = rd2<T>(__ffma2_rn(rd2<T>(f2(hp.omb1, hp.omb2)), pooled, rd2<T>(__fmul2_rn(mv, f2(hp.beta1, hp.beta2)))));
     row[j] = mv;
@@ -382,6 +402,7 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
     const float wd = rd<T>(d.hp.weight_decay);  // add(p, alpha=wd): alpha in the tensor's dtype
     for (int j0 = threadIdx.x; j0 < w; j0 += CELLS * NT) {
         float gv[CELLS][KH][KW], pv[CELLS][KH][KW];
+        OldCell old[CELLS];
 #pragma unroll
         for (int u = 0; u < CELLS; u++) {
             const int j = j0 + u * NT;
@@ -392,6 +413,7 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
 #pragma unroll
                     for (int i = 0; i < KH; i++) load_row<T, KW, kParam>(pb + i * W + (int64_t)j * KW, pv[u][i]);
                 }
+                old[u] = load_old<T>(d, cell0 + j);
             }
         }
         {
@@ -409,7 +431,8 @@ __device__ __forceinline__ void phase1_wd(const FusedDesc &d, int c, float2 *row
 #pragma unroll
         for (int u = 0; u < CELLS; u++) {
             const int j = j0 + u * NT;
-            if (u == 0 || j < w) ema_cell<T>(d, cell0 + j, pool_cell<T, KH, KW, WD>(gv[u], pv[u], wd), row, j, own);
+            if (u == 0 || j < w)
+                ema_cell<T>(d, cell0 + j, old[u], pool_cell<T, KH, KW, WD>(gv[u], pv[u], wd), row, j, own);
         }
     }
 }
